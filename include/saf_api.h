@@ -1,0 +1,137 @@
+/*
+ * saf_api.h -- C ABI of the B200 (sm_100a) sparse-attention hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as `void*`, a cudaStream_t), returns a saf_status, allocates no
+ * device memory and never synchronises the device (except the functions
+ * documented as synchronising).  All work is enqueued on the given stream.
+ *
+ * The reference (xiaolong-li1/SparseAttnFunctions, Python + Triton) has no
+ * FFI; the Python host package `sparseattnfunctions_b200.special_attentions`
+ * binds these symbols with ctypes and keeps the reference's Python names.
+ * Each declaration below names the reference function whose work it
+ * replaces (path:line inside the reference project).
+ *
+ * Tensor convention: q, k, v, o are [B, H, S, D] ("HND") with element
+ * strides; the D stride must be 1.
+ */
+#ifndef SAF_API_H
+#define SAF_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SAF_ABI_VERSION 1
+
+typedef enum saf_status {
+  SAF_OK = 0,
+  SAF_ERR_SHAPE = 1,       /* inconsistent or unsupported sizes */
+  SAF_ERR_DTYPE = 2,       /* unsupported or mismatched element type */
+  SAF_ERR_STRIDE = 3,      /* bad stride or pointer alignment */
+  SAF_ERR_CUDA = 4,        /* a CUDA runtime call failed */
+  SAF_ERR_TIMEOUT = 5,     /* a device-side wait ran out of its budget */
+  SAF_ERR_NCCL = 6,        /* reserved for the collective layer */
+  SAF_ERR_ARG = 7,         /* null pointer or bad scalar argument */
+  SAF_ERR_UNSUPPORTED = 8, /* device is not sm_100 or config has no kernel */
+  SAF_ERR_WORKSPACE = 9    /* workspace missing or too small */
+} saf_status;
+
+typedef enum saf_dtype { SAF_BF16 = 0, SAF_F16 = 1, SAF_F32 = 2 } saf_dtype;
+
+/* Device status flags (sticky, per device; read with saf_read_device_status). */
+#define SAF_DEV_TIMEOUT 0x1u   /* an mbarrier wait gave up */
+#define SAF_DEV_BADINDEX 0x2u  /* a CSR column index was out of range and skipped */
+
+/* A [B, H, S, D] tensor view in device memory (strides in elements). */
+typedef struct saf_tensor4 {
+  void* data;
+  int32_t dtype; /* saf_dtype */
+  int32_t reserved;
+  int64_t B, H, S, D;
+  int64_t stride_b, stride_h, stride_s; /* stride_d == 1 */
+} saf_tensor4;
+
+/* Block-selection settings for saf_pool_topk. */
+typedef struct saf_select_cfg {
+  int32_t block_m;            /* query rows per mask block (64 or 128) */
+  int32_t block_n;            /* key rows per mask block (64 or 128)   */
+  int32_t topk;               /* blocks kept per row by pooled score   */
+  int32_t text_blocks_q;      /* row blocks [0, text_blocks_q) are dense */
+  int32_t text_blocks_k;      /* columns [0, text_blocks_k) live in every row */
+  int32_t force_diag;         /* 1: column i is live in row i            */
+  int32_t forced_inside_topk; /* 1: forced columns count toward topk     */
+  int32_t reserved;
+} saf_select_cfg;
+
+/* ---- library / device ---------------------------------------------- */
+
+int32_t saf_abi_version(void);
+const char* saf_status_string(int32_t status);
+/* SAF_OK when `device` is an sm_100 GPU the kernels were built for. */
+int32_t saf_device_check(int32_t device);
+/* Budget of every device-side mbarrier wait, in nanoseconds (default 1 s).
+ * A wait that runs out sets SAF_DEV_TIMEOUT and the kernel returns early; a
+ * wait that is still pending while that flag is set gives up as well. */
+void saf_set_wait_budget_ns(uint64_t ns);
+uint64_t saf_get_wait_budget_ns(void);
+/* Synchronises `device`, returns its sticky status flags, clears them if
+ * `clear` is non-zero.  Not for the hot path. */
+int32_t saf_read_device_status(int32_t device, uint32_t* flags_out, int32_t clear);
+
+/* ---- (1) block selection --------------------------------------------
+ * Mean-pools q and k per block (fp64), scores the pooled blocks
+ * (q_mean . k_mean, fp64, ascending d), keeps the top-k columns of every
+ * row block (ties: lower column first), forces text rows/columns (and the
+ * diagonal when asked) and writes a segmented CSR:
+ *   row_ptr [B*H, nbq+1] int32, absolute offsets into col_idx;
+ *   head g's entries lie in [g*nbq*nbk, (g+1)*nbq*nbk) (col_idx capacity
+ *   B*H*nbq*nbk), columns ascending within a row.
+ * mask_out [B*H, nbq, nbk] uint8 and score_out [B*H, nbq, nbk] fp64 are
+ * optional (NULL to skip).
+ * Replaces: calc_attn_block_sum_efficient (utils/mask_related.py:40-81),
+ * get_sparse_attn_mask_from_topk (utils/block_sparse_attn_kernel.py:31-39),
+ * the forced text rows/columns of transfer_attn_to_mask
+ * (SparseGen_Plus.py:81-82) and get_block_mask's dense padding
+ * (utils/mask_related.py:402-403). */
+size_t saf_pool_topk_workspace_bytes(const saf_tensor4* q, const saf_tensor4* k,
+                                     const saf_select_cfg* cfg);
+int32_t saf_pool_topk(const saf_tensor4* q, const saf_tensor4* k, const saf_select_cfg* cfg,
+                      int32_t* row_ptr, int32_t* col_idx, uint8_t* mask_out, double* score_out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dense boolean block mask [BH, nbq, nbk] (uint8, element strides
+ * stride_bh / stride_row, column stride 1) -> segmented CSR as above.
+ * Replaces the dense-mask walk of _fwd_kernel
+ * (utils/block_sparse_attn_kernel.py:167-199), which reads every mask bit. */
+int32_t saf_mask_to_csr(const uint8_t* mask, int64_t BH, int32_t nbq, int32_t nbk,
+                        int64_t stride_bh, int64_t stride_row, int32_t* row_ptr,
+                        int32_t* col_idx, void* stream);
+
+/* ---- (2) block-sparse attention -------------------------------------
+ * o[b,h,i,:] = sum_{j live} softmax_j(sm_scale * q_i . k_j + bias_j) v_j
+ * over the key blocks listed in the CSR row of query block i / block_m.
+ * bf16 / f16: tcgen05 + TMEM + TMA kernel (D = 64), fp32 accumulation,
+ * output in the input type.  f32: CUDA-core kernel in full fp32.
+ * kv_bias (nullable): fp32 additive bias per key column, read at
+ * kv_bias[g * kv_bias_stride_bh + j] for head g = b*H + h (stride 0
+ * broadcasts one row).  Rows with no live block give NaN (0/0), as the
+ * reference kernel does.
+ * col_capacity bounds every col_idx read (entries past it are ignored).
+ * Replaces: _forward / _fwd_kernel / _fwd_kernel_inner /
+ * block_sparse_triton_fn (utils/block_sparse_attn_kernel.py:52-293) and the
+ * bias path of MergeAttention.forward (MergeAttention.py:33-49). */
+int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                    const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
+                    int64_t col_capacity, int32_t block_m, int32_t block_n,
+                    const float* kv_bias, int64_t kv_bias_stride_bh, float sm_scale,
+                    void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SAF_API_H */

@@ -1,0 +1,595 @@
+// bsa_sm100.cu -- block-sparse flash attention for sm_100a (B200).
+//
+// Computes, for every query row i of head g = b*H + h,
+//   o_i = sum_{j in live kv blocks} softmax_j(sm_scale * q_i . k_j + bias_j) v_j
+// where the live kv blocks of query block i / block_m come from a CSR list.
+// Semantics follow the reference Triton kernel
+// (special_attentions/utils/block_sparse_attn_kernel.py:52-209): online
+// softmax, fp32 statistics and accumulation, P rounded to the input type
+// before the PV product, keys past seqlen_k masked to -inf (:74-89), and
+// a row with no live block divided by a zero row sum (:201-203).  Unlike the
+// reference, which walks every mask bit of a row (:167-199), only the listed
+// blocks are visited.
+//
+// Design (one CTA = 128 query rows of one head, 2 CTAs per SM):
+//   warp 0      TMA producer: Q once, then K / V tiles of each live block
+//               (3-stage K ring, 2-stage V ring, 128B swizzle), plus the
+//               optional per-column bias (plain loads into shared memory).
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer:
+//               S = Q K^T (SS form) into TMEM, then O += P V (TS form, P read
+//               from TMEM) for the previous block.
+//   warps 2..5  softmax: one thread per query row (= TMEM lane).  Reads S
+//               from TMEM twice (row max, then exp2 per 32-column chunk, so
+//               only 32 scores are live in registers), keeps the running max
+//               m and sum l in registers, writes P (bf16/f16 pairs) into TMEM
+//               and rescales the O accumulator in TMEM only when a row's max
+//               grows by more than 2^8 (so P <= 256; exact after 1/l).
+// TMEM columns: S [0,128) | O [128,192) | P [192,256).
+//
+// Every mbarrier wait has a time budget; on expiry the CTA raises a shared
+// abort flag and the device status word, drains the copies and MMAs it has in
+// flight, frees TMEM and returns.
+#include "saf_common.cuh"
+
+namespace saf {
+namespace {
+
+constexpr int kBM = 128;       // query rows per CTA
+constexpr int kD = 64;         // head dim handled by this kernel
+constexpr int kKS = 3;         // K stages
+constexpr int kVS = 2;         // V stages
+constexpr int kThreads = 192;  // 6 warps
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0, kColO = 128, kColP = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct BsaParams {
+  int B, H, Sq, Sk;
+  int nbq, nbk;    // mask rows / columns
+  int bm;          // mask block rows: 64 or 128
+  int64_t col_capacity;
+  const int32_t* row_ptr;  // [B*H, nbq+1]
+  const int32_t* col_idx;
+  const float* kv_bias;    // nullable
+  int64_t bias_stride;     // per head, elements
+  float scale_log2;        // sm_scale * log2(e)
+  void* o;
+  int64_t o_sb, o_sh, o_ss;  // element strides
+  unsigned int* status;
+  uint64_t budget_ns;
+};
+
+// Iterates the live kv tiles of one 128-row query tile.  With 64-row mask
+// blocks the tile covers two mask rows; their (ascending) column lists are
+// merged and every tile carries a 2-bit row mask: bit 0 = rows [0,64) live,
+// bit 1 = rows [64,128) live.  Every role of the CTA runs its own copy, so
+// all of them see the same sequence.  Out-of-range columns are skipped.
+struct TileIter {
+  const int32_t* cols;
+  int64_t p0, e0, p1, e1;
+  int nbk;
+  bool two_rows;
+  unsigned int* status;
+
+  __device__ void init(const BsaParams& p, int g, int tile) {
+    cols = p.col_idx;
+    nbk = p.nbk;
+    status = p.status;
+    const int32_t* rp = p.row_ptr + static_cast<int64_t>(g) * (p.nbq + 1);
+    auto clampi = [&](int64_t x) {
+      return x < 0 ? int64_t(0) : (x > p.col_capacity ? p.col_capacity : x);
+    };
+    two_rows = (p.bm == 64);
+    const int r0 = two_rows ? 2 * tile : tile;
+    p0 = clampi(rp[r0]);
+    e0 = clampi(rp[r0 + 1]);
+    p1 = e1 = 0;
+    if (two_rows && r0 + 1 < p.nbq) {
+      p1 = clampi(rp[r0 + 1]);
+      e1 = clampi(rp[r0 + 2]);
+    }
+  }
+  __device__ bool valid(int c) {
+    if (c >= 0 && c < nbk) return true;
+    atomicOr(status, SAF_DEV_BADINDEX);
+    return false;
+  }
+  __device__ bool next(int& col, uint32_t& rmask) {
+    while (true) {
+      const bool h0 = p0 < e0, h1 = p1 < e1;
+      if (!h0 && !h1) return false;
+      int c;
+      uint32_t m;
+      if (!two_rows) {
+        c = cols[p0++];
+        m = 3u;
+      } else {
+        const int c0 = h0 ? cols[p0] : 0x7fffffff;
+        const int c1 = h1 ? cols[p1] : 0x7fffffff;
+        if (c0 <= c1) {
+          c = c0;
+          m = 1u;
+          ++p0;
+          if (c1 == c0) {
+            m |= 2u;
+            ++p1;
+          }
+        } else {
+          c = c1;
+          m = 2u;
+          ++p1;
+        }
+      }
+      if (valid(c)) {
+        col = c;
+        rmask = m;
+        return true;
+      }
+    }
+  }
+};
+
+template <int BN>
+struct Layout {
+  static constexpr int kQBytes = kBM * kD * 2;  // 16 KB
+  static constexpr int kKVBytes = BN * kD * 2;  // 16 / 8 KB
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffV = kOffK + kKS * kKVBytes;
+  static constexpr int kOffBias = kOffV + kVS * kKVBytes;
+  static constexpr int kOffBar = kOffBias + kVS * BN * 4;
+  // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
+  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain
+  static constexpr int kNumBars = 1 + 2 * kKS + 3 * kVS + 5;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kBytes = kOffMisc + 16;
+  static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
+};
+
+template <int BN, bool kBias, bool kBF16>
+__global__ void __launch_bounds__(kThreads, 2)
+    bsa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const BsaParams p) {
+  using L = Layout<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int g = blockIdx.y;
+  const int b = g / p.H, h = g % p.H;
+  const int q0 = tile * kBM;
+
+  const uint32_t sQ = smem_u32(smem + L::kOffQ);
+  const uint32_t sK0 = smem_u32(smem + L::kOffK);
+  const uint32_t sV0 = smem_u32(smem + L::kOffV);
+  float* sBias = reinterpret_cast<float*>(smem + L::kOffBias);
+  const uint32_t bar0 = smem_u32(smem + L::kOffBar);
+  const uint32_t bar_q = bar0;
+  auto bar_k_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto bar_k_empty = [&](int s) { return bar0 + 8u * (1 + kKS + s); };
+  auto bar_v_full = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + s); };
+  auto bar_v_empty = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + kVS + s); };
+  auto bar_b_full = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + 2 * kVS + s); };
+  const uint32_t bar_s_full = bar0 + 8u * (1 + 2 * kKS + 3 * kVS);
+  const uint32_t bar_s_empty = bar_s_full + 8;
+  const uint32_t bar_p_full = bar_s_full + 16;
+  const uint32_t bar_pv_full = bar_s_full + 24;
+  const uint32_t bar_drain = bar_s_full + 32;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < kKS; ++s) {
+      mbar_init(bar_k_full(s), 1);
+      mbar_init(bar_k_empty(s), 1);
+    }
+    for (int s = 0; s < kVS; ++s) {
+      mbar_init(bar_v_full(s), 1);
+      mbar_init(bar_v_empty(s), 1);
+      mbar_init(bar_b_full(s), 32);
+    }
+    mbar_init(bar_s_full, 1);
+    mbar_init(bar_s_empty, 128);
+    mbar_init(bar_p_full, 128);
+    mbar_init(bar_pv_full, 1);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar_q, L::kQBytes);
+      tma_load_4d(sQ, &tm_q, bar_q, 0, q0, h, b);
+    }
+    TileIter it;
+    it.init(p, g, tile);
+    int nk = 0, nv = 0, col;  // K / V loads issued so far
+    uint32_t rm;
+    while (it.next(col, rm)) {
+      const int sk = nk % kKS, sv = nv % kVS;
+      const uint32_t pk = (nk / kKS) & 1, pv = (nv / kVS) & 1;
+      bool ok = mbar_wait(bar_k_empty(sk), pk ^ 1, abort_flag, p.status, p.budget_ns);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_k_full(sk), L::kKVBytes);
+        tma_load_4d(sK0 + sk * L::kKVBytes, &tm_k, bar_k_full(sk), 0, col * BN, h, b);
+      }
+      ++nk;
+      ok = mbar_wait(bar_v_empty(sv), pv ^ 1, abort_flag, p.status, p.budget_ns);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
+        tma_load_4d(sV0 + sv * L::kKVBytes, &tm_v, bar_v_full(sv), 0, col * BN, h, b);
+      }
+      ++nv;
+      if constexpr (kBias) {
+        const float* src = p.kv_bias + static_cast<int64_t>(g) * p.bias_stride;
+        float* dst = sBias + sv * BN;
+        for (int c = lane; c < BN; c += 32) {
+          const int kv = col * BN + c;
+          dst[c] = kv < p.Sk ? src[kv] * kLog2e : 0.f;
+        }
+        mbar_arrive(bar_b_full(sv));
+      }
+    }
+    // Drain: wait for the last load issued into every stage (and so for all
+    // earlier ones).  Immediate on the normal path, where the consumers have
+    // already seen every load land.
+    if (lane == 0) {
+      mbar_drain(bar_q, 0, p.status);
+      for (int s = 0; s < kKS && s < nk; ++s) {
+        const int last = s + ((nk - 1 - s) / kKS) * kKS;
+        mbar_drain(bar_k_full(s), (last / kKS) & 1, p.status);
+      }
+      for (int s = 0; s < kVS && s < nv; ++s) {
+        const int last = s + ((nv - 1 - s) / kVS) * kVS;
+        mbar_drain(bar_v_full(s), (last / kVS) & 1, p.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescQK = idesc_f16(kBM, BN, kBF16, false, false);
+      constexpr uint32_t kIdescPV = idesc_f16(kBM, kD, kBF16, false, true);
+      const uint32_t tS = tmem + kColS, tO = tmem + kColO, tP = tmem + kColP;
+      bool ok = mbar_wait(bar_q, 0, abort_flag, p.status, p.budget_ns);
+      tc_fence_after();
+
+      auto issue_pv = [&](int i) -> bool {
+        const int sv = i % kVS;
+        const uint32_t pv = (i / kVS) & 1;
+        if (!mbar_wait(bar_v_full(sv), pv, abort_flag, p.status, p.budget_ns)) return false;
+        if (!mbar_wait(bar_p_full, i & 1, abort_flag, p.status, p.budget_ns)) return false;
+        tc_fence_after();
+        const uint32_t vbase = sV0 + sv * L::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          // B = V^T: N = D (contiguous, one 128B swizzle atom), K = kv rows;
+          // 16 kv rows = two 8-row atoms = 2048 bytes.
+          const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, L::kKVBytes, 1024);
+          tc_mma_ts(tO, tP + kk * 8, bdesc, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(bar_pv_full);
+        tc_commit(bar_v_empty(sv));
+        return true;
+      };
+
+      TileIter it;
+      it.init(p, g, tile);
+      int j = 0, col;
+      uint32_t rm;
+      bool finished = false;
+      while (ok) {
+        if (!it.next(col, rm)) {
+          finished = true;
+          break;
+        }
+        const int sk = j % kKS;
+        const uint32_t pk = (j / kKS) & 1;
+        if (!mbar_wait(bar_k_full(sk), pk, abort_flag, p.status, p.budget_ns)) break;
+        if (!mbar_wait(bar_s_empty, (j & 1) ^ 1, abort_flag, p.status, p.budget_ns)) break;
+        tc_fence_after();
+        const uint32_t kbase = sK0 + sk * L::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          // K-major, 128B swizzle: 16 elements of K = 32 bytes along the row.
+          const uint64_t adesc = sdesc_sw128(sQ + kk * 32, 16, 1024);
+          const uint64_t bdesc = sdesc_sw128(kbase + kk * 32, 16, 1024);
+          tc_mma_ss(tS, adesc, bdesc, kIdescQK, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(bar_s_full);
+        tc_commit(bar_k_empty(sk));
+        if (j > 0 && !issue_pv(j - 1)) break;
+        ++j;
+      }
+      if (finished && j > 0) issue_pv(j - 1);
+      tc_commit(bar_drain);
+      mbar_drain(bar_drain, 0, p.status);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t half = static_cast<uint32_t>(row >> 6);
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + kColS;
+    const uint32_t tO = tmem + lane_addr + kColO;
+    const uint32_t tP = tmem + lane_addr + kColP;
+    const float sl2 = p.scale_log2;
+
+    float m_run = -INFINITY, l_run = 0.f;
+    TileIter it;
+    it.init(p, g, tile);
+    int j = 0, col;
+    uint32_t rm;
+    bool ok = true;
+    while (it.next(col, rm)) {
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(bar_s_full, j & 1, abort_flag, p.status, p.budget_ns))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool live = (rm >> half) & 1u;
+      const int valid = p.Sk - col * BN;
+      const float* bb = sBias + (j % kVS) * BN;
+      if constexpr (kBias) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_b_full(j % kVS), (j / kVS) & 1, abort_flag,
+                                                p.status, p.budget_ns))) {
+          ok = false;
+          break;
+        }
+      }
+      // Loads 32 scores of chunk c as log2-domain logits (bias added when
+      // present, otherwise still unscaled) with masked entries = -inf.
+      auto load_chunk = [&](int c, float (&t)[32]) {
+        uint32_t r[32];
+        tmem_ld32(tS + c * 32, r);
+        tmem_wait_ld(r);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int cc = c * 32 + e;
+          float x = __uint_as_float(r[e]);
+          if constexpr (kBias) x = fmaf(x, sl2, bb[cc]);
+          t[e] = (live && cc < valid) ? x : -INFINITY;
+        }
+      };
+
+      // Pass 1: row max.
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32];
+        load_chunk(c, t);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, t[e]);
+        // Keep each chunk's reduction ahead of the next TMEM load (bounds the
+        // number of live scores to one chunk).
+        asm volatile("" : "+f"(mx));
+      }
+      const float m_cand = kBias ? mx : mx * sl2;
+      const bool upd = m_cand > m_run + kRescaleThreshold;
+      const float m_new = upd ? m_cand : m_run;
+      const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
+      const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
+
+      if (j > 0) {
+        // PV of the previous block must be done before P is overwritten and
+        // before O is rescaled.
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status,
+                                                p.budget_ns))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, upd)) {
+#pragma unroll
+          for (int c = 0; c < kD / 32; ++c) {
+            uint32_t orr[32];
+            tmem_ld32(tO + c * 32, orr);
+            tmem_wait_ld(orr);
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+            tmem_st32(tO + c * 32, orr);
+          }
+        }
+      }
+
+      // Pass 2: P = exp2(logit - m) in the input type, row sum in fp32.
+      float rs0 = 0.f, rs1 = 0.f;
+// Not unrolled: keeps the next chunk's TMEM load from being hoisted over
+      // this chunk's exp2 work (which would hold 2 chunks in registers).
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float t[32];
+        load_chunk(c, t);
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float e0, e1;
+          if constexpr (kBias) {
+            e0 = ex2_approx(t[2 * e] + neg_m);
+            e1 = ex2_approx(t[2 * e + 1] + neg_m);
+          } else {
+            e0 = ex2_approx(fmaf(t[2 * e], sl2, neg_m));
+            e1 = ex2_approx(fmaf(t[2 * e + 1], sl2, neg_m));
+          }
+          rs0 += e0;
+          rs1 += e1;
+          pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
+        }
+        tmem_st16(tP + c * 16, pk);
+        asm volatile("" : "+f"(rs0), "+f"(rs1));
+      }
+      // S has been read for the last time: the next QK^T may overwrite it.
+      tc_fence_before();
+      mbar_arrive(bar_s_empty);
+      l_run = l_run * alpha + (rs0 + rs1);
+      m_run = m_new;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_p_full);
+      ++j;
+    }
+
+    // ---------------------------------------------------------- epilogue
+    // O is read back 32 columns at a time, normalised by 1/l and stored.
+    // A zero row sum gives 0 * inf = NaN, matching the reference; a tile with
+    // no live block never wrote O and stores 0 * inf = NaN as well.
+    const bool have_o =
+        ok && j > 0 &&
+        __all_sync(0xffffffffu,
+                   mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status, p.budget_ns));
+    if (have_o) tc_fence_after();
+    const int qrow = q0 + row;
+    const float inv_l = 1.f / l_run;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
+                   2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
+                        static_cast<int64_t>(qrow) * p.o_ss);
+    const bool write = (j == 0 || have_o) && !*abort_flag && qrow < p.Sq;
+#pragma unroll
+    for (int c = 0; c < kD / 32; ++c) {
+      uint32_t orr[32];
+      if (have_o) {
+        tmem_ld32(tO + c * 32, orr);
+        tmem_wait_ld(orr);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) orr[e] = 0u;
+      }
+      if (write) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float lo = __uint_as_float(orr[v * 8 + 2 * e]) * inv_l;
+            const float hi = __uint_as_float(orr[v * 8 + 2 * e + 1]) * inv_l;
+            pw[e] = kBF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+          }
+          reinterpret_cast<uint4*>(dst)[c * 4 + v] = w;
+        }
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Builds a 4-D tensor map over a [B,H,S,D] 16-bit tensor with a box of
+// `rows` x 64 elements and 128-byte swizzle.
+int32_t make_qkv_map(CUtensorMap* map, const saf_tensor4* t, int rows) {
+  const uint64_t eb = 2;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t->D), static_cast<cuuint64_t>(t->S),
+                        static_cast<cuuint64_t>(t->H), static_cast<cuuint64_t>(t->B)};
+  uint64_t sh = static_cast<uint64_t>(t->stride_h), sb = static_cast<uint64_t>(t->stride_b);
+  // Extent-1 dims take any legal stride.
+  if (t->H == 1) sh = static_cast<uint64_t>(t->stride_s) * t->S;
+  if (t->B == 1) sb = sh * t->H;
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t->stride_s) * eb, sh * eb, sb * eb};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16 != 0 || strides[i] == 0 || strides[i] >= (1ull << 40))
+      return SAF_ERR_STRIDE;
+  cuuint32_t box[4] = {64u, static_cast<cuuint32_t>(rows), 1u, 1u};
+  const CUtensorMapDataType dt =
+      t->dtype == SAF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode_tensor_map(map, dt, 4, t->data, dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  return r == CUDA_SUCCESS ? SAF_OK : SAF_ERR_STRIDE;
+}
+
+template <int BN, bool kBias, bool kBF16>
+int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                       const BsaParams& p, int n_tiles, cudaStream_t stream) {
+  auto kern = bsa_fwd_sm100_kernel<BN, kBias, kBF16>;
+  const int smem = Layout<BN>::kDynSmem;
+  SAF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(n_tiles, p.B * p.H);
+  kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}
+
+}  // namespace
+
+// Host entry for 16-bit inputs (validated by the caller in saf_api.cu).
+int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                      const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
+                      int64_t col_capacity, int bm, int bn, const float* kv_bias,
+                      int64_t bias_stride, float sm_scale, cudaStream_t stream) {
+  if (q->D != kD) return SAF_ERR_UNSUPPORTED;
+  if (!current_device_is_sm100()) return SAF_ERR_UNSUPPORTED;
+  CUtensorMap mq, mk, mv;
+  int32_t rc;
+  if ((rc = make_qkv_map(&mq, q, kBM)) != SAF_OK) return rc;
+  if ((rc = make_qkv_map(&mk, k, bn)) != SAF_OK) return rc;
+  if ((rc = make_qkv_map(&mv, v, bn)) != SAF_OK) return rc;
+  BsaParams p{};
+  p.B = static_cast<int>(q->B);
+  p.H = static_cast<int>(q->H);
+  p.Sq = static_cast<int>(q->S);
+  p.Sk = static_cast<int>(k->S);
+  p.bm = bm;
+  p.nbq = static_cast<int>((q->S + bm - 1) / bm);
+  p.nbk = static_cast<int>((k->S + bn - 1) / bn);
+  p.col_capacity = col_capacity;
+  p.row_ptr = row_ptr;
+  p.col_idx = col_idx;
+  p.kv_bias = kv_bias;
+  p.bias_stride = bias_stride;
+  p.scale_log2 = sm_scale * kLog2e;
+  p.o = o->data;
+  p.o_sb = o->stride_b;
+  p.o_sh = o->stride_h;
+  p.o_ss = o->stride_s;
+  p.status = device_status_ptr();
+  p.budget_ns = wait_budget_ns();
+  if (p.status == nullptr) return SAF_ERR_CUDA;
+  const int n_tiles = static_cast<int>((q->S + kBM - 1) / kBM);
+  const bool bf16 = q->dtype == SAF_BF16;
+  const bool bias = kv_bias != nullptr;
+#define SAF_BSA_CASE(BN_, BIAS_, BF_)                                 \
+  if (bn == BN_ && bias == BIAS_ && bf16 == BF_)                      \
+    return launch_variant<BN_, BIAS_, BF_>(mq, mk, mv, p, n_tiles, stream);
+  SAF_BSA_CASE(128, false, true)
+  SAF_BSA_CASE(128, true, true)
+  SAF_BSA_CASE(128, false, false)
+  SAF_BSA_CASE(128, true, false)
+  SAF_BSA_CASE(64, false, true)
+  SAF_BSA_CASE(64, true, true)
+  SAF_BSA_CASE(64, false, false)
+  SAF_BSA_CASE(64, true, false)
+#undef SAF_BSA_CASE
+  return SAF_ERR_UNSUPPORTED;
+}
+
+}  // namespace saf

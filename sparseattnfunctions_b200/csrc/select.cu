@@ -1,0 +1,438 @@
+// select.cu -- block selection: mean-pool q and k per block, score the pooled
+// blocks, keep the top-k columns per row block, force text rows / columns,
+// and emit a segmented CSR.  Also the dense-mask -> CSR conversion.
+//
+// Numerics contract (shared with the CPU oracle, oracle/selection.py):
+//   * block means: fp64 sum of the block's rows (exact for realistic data:
+//     bf16 / f16 values summed in fp64 lose nothing unless the block spans
+//     more than ~2^40 in magnitude), divided by the valid row count
+//     (IEEE division);
+//   * score[i][j] = sum_d q_mean[i][d] * k_mean[j][d] in fp64, d ascending,
+//     every product and every sum rounded separately (no FMA contraction);
+//   * top-k order: higher score first, equal scores -> lower column first.
+// With these rules the GPU and the oracle select bit-identical blocks.
+//
+// Reference counterparts: calc_attn_block_sum_efficient
+// (special_attentions/utils/mask_related.py:40-81) pools a random 8-of-64
+// token sample per block; the deterministic mean-pool replaces it.
+// get_sparse_attn_mask_from_topk (utils/block_sparse_attn_kernel.py:31-39)
+// is the top-k rule; transfer_attn_to_mask (SparseGen_Plus.py:81-82) and
+// get_block_mask (utils/mask_related.py:402-403) force the text blocks.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "saf_common.cuh"
+
+namespace saf {
+namespace {
+
+constexpr int kPoolThreads = 256;
+constexpr int kMaxM = 16;  // column slots per lane: nbk <= 512
+constexpr int kRowsPerCta = 16;
+constexpr int kDChunk = 32;
+
+__device__ __forceinline__ double to_f64(__nv_bfloat16 x) {
+  return static_cast<double>(__bfloat162float(x));
+}
+__device__ __forceinline__ double to_f64(__half x) { return static_cast<double>(__half2float(x)); }
+__device__ __forceinline__ double to_f64(float x) { return static_cast<double>(x); }
+
+// grid (nb, B*H); mean over the rows of one block, fp64.
+template <typename T>
+__global__ void __launch_bounds__(kPoolThreads) pool_mean_kernel(
+    const T* __restrict__ x, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int block,
+    double* __restrict__ out) {
+  constexpr int VEC = 16 / sizeof(T);
+  extern __shared__ double part[];  // [groups][D]
+  const int blk = blockIdx.x, g = blockIdx.y;
+  const int b = g / H, h = g % H;
+  const int r0 = blk * block;
+  const int nrows = min(block, S - r0);
+  const int vpr = D / VEC;                 // vectors per row
+  const int groups = kPoolThreads / vpr;   // rows processed in parallel
+  const int tid = threadIdx.x;
+  const int vc = tid % vpr, rg = tid / vpr;
+  const T* base = x + static_cast<int64_t>(b) * sb + static_cast<int64_t>(h) * sh;
+  double acc[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) acc[e] = 0.0;
+  if (rg < groups) {
+    for (int r = rg; r < nrows; r += groups) {
+      const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<int64_t>(r0 + r) * ss +
+                                                      vc * VEC);
+      const T* pv = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] += to_f64(pv[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) part[rg * D + vc * VEC + e] = acc[e];
+  }
+  __syncthreads();
+  for (int d = tid; d < D; d += kPoolThreads) {
+    double s = 0.0;
+    for (int k = 0; k < groups; ++k) s += part[k * D + d];
+    out[(static_cast<int64_t>(g) * gridDim.x + blk) * D + d] = s / static_cast<double>(nrows);
+  }
+}
+
+struct SelectArgs {
+  int nbq, nbk, D;
+  int topk, text_q, text_k, force_diag, forced_inside;
+  const double* qbar;  // [BH, nbq, D]
+  const double* kbar;  // [BH, nbk, D]
+  int32_t* padded;     // [BH, nbq, nbk]
+  int32_t* counts;     // [BH, nbq]
+  uint8_t* mask_out;   // nullable [BH, nbq, nbk]
+  double* score_out;   // nullable [BH, nbq, nbk]
+};
+
+__device__ __forceinline__ bool better(double a, int ia, double b, int ib) {
+  return a > b || (a == b && ia < ib);
+}
+
+// grid (B*H, ceil(nbq / kRowsPerCta)), 256 threads; one warp per row.
+__global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
+  extern __shared__ double ks[];  // [nbk][kDChunk+1] then [kRowsPerCta][kDChunk+1]
+  double* qs = ks + a.nbk * (kDChunk + 1);
+  const int g = blockIdx.x;
+  const int row_base = blockIdx.y * kRowsPerCta;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = (a.nbk + 31) / 32;
+  constexpr int kRowsPerWarp = kRowsPerCta / 8;
+
+  double sc[kRowsPerWarp][kMaxM];
+#pragma unroll
+  for (int rr = 0; rr < kRowsPerWarp; ++rr)
+#pragma unroll
+    for (int m = 0; m < kMaxM; ++m) sc[rr][m] = 0.0;
+
+  const double* kb = a.kbar + static_cast<int64_t>(g) * a.nbk * a.D;
+  const double* qb = a.qbar + static_cast<int64_t>(g) * a.nbq * a.D;
+  for (int d0 = 0; d0 < a.D; d0 += kDChunk) {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < a.nbk * kDChunk; idx += blockDim.x) {
+      const int j = idx / kDChunk, d = idx % kDChunk;
+      ks[j * (kDChunk + 1) + d] = kb[static_cast<int64_t>(j) * a.D + d0 + d];
+    }
+    for (int idx = threadIdx.x; idx < kRowsPerCta * kDChunk; idx += blockDim.x) {
+      const int r = idx / kDChunk, d = idx % kDChunk;
+      const int row = row_base + r;
+      qs[r * (kDChunk + 1) + d] = row < a.nbq ? qb[static_cast<int64_t>(row) * a.D + d0 + d] : 0.0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+      const int r = warp * kRowsPerWarp + rr;
+#pragma unroll
+      for (int m = 0; m < kMaxM; ++m) {
+        const int j = lane + 32 * m;
+        if (m < M && j < a.nbk) {
+          double s = sc[rr][m];
+          for (int d = 0; d < kDChunk; ++d)
+            s = __dadd_rn(s, __dmul_rn(qs[r * (kDChunk + 1) + d], ks[j * (kDChunk + 1) + d]));
+          sc[rr][m] = s;
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+    const int row = row_base + warp * kRowsPerWarp + rr;
+    if (row >= a.nbq) continue;
+    const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
+    uint32_t forced = 0, eligible = 0, sel = 0;  // bit m <-> column lane + 32m
+    int nforced = 0;
+    const bool text_row = row < a.text_q;
+#pragma unroll
+    for (int m = 0; m < kMaxM; ++m) {
+      const int j = lane + 32 * m;
+      if (m < M && j < a.nbk) {
+        const bool f = text_row || j < a.text_k || (a.force_diag && j == row);
+        if (f) forced |= 1u << m;
+        if (!(f && a.forced_inside)) eligible |= 1u << m;
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < kMaxM; ++m) nforced += __popc(__ballot_sync(0xffffffffu, (forced >> m) & 1u));
+    int krem = a.forced_inside ? a.topk - nforced : a.topk;
+    if (text_row) krem = 0;
+    for (int round = 0; round < krem; ++round) {
+      double best = -INFINITY;
+      int bj = 0x7fffffff;
+#pragma unroll
+      for (int m = 0; m < kMaxM; ++m) {
+        if (((eligible & ~sel) >> m) & 1u) {
+          const int j = lane + 32 * m;
+          if (better(sc[rr][m], j, best, bj)) {
+            best = sc[rr][m];
+            bj = j;
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+        if (better(ob, oj, best, bj)) {
+          best = ob;
+          bj = oj;
+        }
+      }
+      if (bj == 0x7fffffff) break;  // no candidate left
+      if ((bj & 31) == lane) sel |= 1u << (bj >> 5);
+    }
+    sel |= forced;
+    int base = 0;
+#pragma unroll
+    for (int m = 0; m < kMaxM; ++m) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (sel >> m) & 1u);
+      if ((sel >> m) & 1u) {
+        const int pos = base + __popc(bal & ((1u << lane) - 1u));
+        a.padded[rbase + pos] = lane + 32 * m;
+      }
+      base += __popc(bal);
+      const int j = lane + 32 * m;
+      if (m < M && j < a.nbk) {
+        if (a.mask_out) a.mask_out[rbase + j] = (sel >> m) & 1u;
+        if (a.score_out) a.score_out[rbase + j] = sc[rr][m];
+      }
+    }
+    if (lane == 0) a.counts[static_cast<int64_t>(g) * a.nbq + row] = base;
+  }
+}
+
+// grid (B*H), 256 threads: per-head exclusive scan of the row counts, then a
+// copy of each row's columns into its CSR slot.
+__global__ void __launch_bounds__(256) csr_compact_kernel(int nbq, int nbk,
+                                                          const int32_t* __restrict__ counts,
+                                                          const int32_t* __restrict__ padded,
+                                                          int32_t* __restrict__ row_ptr,
+                                                          int32_t* __restrict__ col_idx) {
+  __shared__ int32_t pref[1025];
+  __shared__ int32_t warp_tot[8];
+  const int g = blockIdx.x;
+  const int64_t seg = static_cast<int64_t>(g) * nbq * nbk;
+  const int32_t* cnt = counts + static_cast<int64_t>(g) * nbq;
+  // nbq <= 1024: each thread scans up to 4 consecutive rows.
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int local[4], tot = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int r = tid * 4 + e;
+    local[e] = r < nbq ? cnt[r] : 0;
+    tot += local[e];
+  }
+  int incl = tot;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int wbase = 0;
+  for (int w = 0; w < warp; ++w) wbase += warp_tot[w];
+  int run = wbase + incl - tot;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int r = tid * 4 + e;
+    if (r < nbq) pref[r] = run;
+    run += local[e];
+  }
+  if (tid == 255) pref[nbq] = run;  // last thread holds the grand total
+  __syncthreads();
+  int32_t* rp = row_ptr + static_cast<int64_t>(g) * (nbq + 1);
+  for (int r = tid; r <= nbq; r += 256) rp[r] = static_cast<int32_t>(seg + pref[r]);
+  for (int r = warp; r < nbq; r += 8) {
+    const int n = pref[r + 1] - pref[r];
+    const int32_t* src = padded + seg + static_cast<int64_t>(r) * nbk;
+    int32_t* dst = col_idx + seg + pref[r];
+    for (int c = lane; c < n; c += 32) dst[c] = src[c];
+  }
+}
+
+// grid (B*H), 512 threads: dense uint8 mask -> segmented CSR for one head.
+// Pass 1 counts every row, a block scan turns counts into offsets, pass 2
+// writes the columns (ascending) at their offsets.
+__global__ void __launch_bounds__(512) mask_to_csr_kernel(const uint8_t* __restrict__ mask,
+                                                          int nbq, int nbk, int64_t s_bh,
+                                                          int64_t s_row, int32_t* __restrict__ row_ptr,
+                                                          int32_t* __restrict__ col_idx) {
+  extern __shared__ int32_t cnt_s[];  // [nbq + 1]
+  const int g = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const uint8_t* mg = mask + static_cast<int64_t>(g) * s_bh;
+  for (int r = warp; r < nbq; r += nwarps) {
+    int c = 0;
+    for (int j0 = 0; j0 < nbk; j0 += 32) {
+      const int j = j0 + lane;
+      c += __popc(__ballot_sync(0xffffffffu, j < nbk && mg[static_cast<int64_t>(r) * s_row + j]));
+    }
+    if (lane == 0) cnt_s[r] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // nbq is small (<= a few hundred): serial scan
+    int run = 0;
+    for (int r = 0; r < nbq; ++r) {
+      const int c = cnt_s[r];
+      cnt_s[r] = run;
+      run += c;
+    }
+    cnt_s[nbq] = run;
+  }
+  __syncthreads();
+  const int64_t seg = static_cast<int64_t>(g) * nbq * nbk;
+  int32_t* rp = row_ptr + static_cast<int64_t>(g) * (nbq + 1);
+  for (int r = threadIdx.x; r <= nbq; r += blockDim.x) rp[r] = static_cast<int32_t>(seg + cnt_s[r]);
+  for (int r = warp; r < nbq; r += nwarps) {
+    int base = cnt_s[r];
+    for (int j0 = 0; j0 < nbk; j0 += 32) {
+      const int j = j0 + lane;
+      const bool on = j < nbk && mg[static_cast<int64_t>(r) * s_row + j];
+      const uint32_t bal = __ballot_sync(0xffffffffu, on);
+      if (on) col_idx[seg + base + __popc(bal & ((1u << lane) - 1u))] = j;
+      base += __popc(bal);
+    }
+  }
+}
+
+struct SelectLayout {
+  size_t off_qbar, off_kbar, off_padded, off_counts, total;
+};
+
+SelectLayout select_layout(int64_t BH, int nbq, int nbk, int D) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  SelectLayout l{};
+  l.off_qbar = 0;
+  l.off_kbar = up(l.off_qbar + static_cast<size_t>(BH) * nbq * D * sizeof(double));
+  l.off_padded = up(l.off_kbar + static_cast<size_t>(BH) * nbk * D * sizeof(double));
+  l.off_counts = up(l.off_padded + static_cast<size_t>(BH) * nbq * nbk * sizeof(int32_t));
+  l.total = up(l.off_counts + static_cast<size_t>(BH) * nbq * sizeof(int32_t));
+  return l;
+}
+
+template <typename T>
+void launch_pool(const saf_tensor4* t, int block, int nb, double* out, cudaStream_t st) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int vpr = static_cast<int>(t->D) / VEC;
+  const int groups = kPoolThreads / vpr;
+  const size_t smem = static_cast<size_t>(groups) * t->D * sizeof(double);
+  dim3 grid(nb, static_cast<unsigned>(t->B * t->H));
+  pool_mean_kernel<T><<<grid, kPoolThreads, smem, st>>>(
+      static_cast<const T*>(t->data), static_cast<int>(t->H), static_cast<int>(t->S),
+      static_cast<int>(t->D), t->stride_b, t->stride_h, t->stride_s, block, out);
+}
+
+int32_t check_pool_operand(const saf_tensor4* t) {
+  int32_t rc = check_tensor4(t);
+  if (rc != SAF_OK) return rc;
+  const int eb = elem_bytes(t->dtype);
+  const int vec = 16 / eb;
+  if (t->D % vec != 0 || t->D > 256 || (kPoolThreads / (t->D / vec)) < 1) return SAF_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(t->data) & 15) != 0) return SAF_ERR_STRIDE;
+  if ((t->stride_s * eb) % 16 != 0 || (t->stride_h * eb) % 16 != 0 || (t->stride_b * eb) % 16 != 0)
+    return SAF_ERR_STRIDE;
+  return SAF_OK;
+}
+
+int32_t pool_dispatch(const saf_tensor4* t, int block, int nb, double* out, cudaStream_t st) {
+  switch (t->dtype) {
+    case SAF_BF16: launch_pool<__nv_bfloat16>(t, block, nb, out, st); break;
+    case SAF_F16: launch_pool<__half>(t, block, nb, out, st); break;
+    case SAF_F32: launch_pool<float>(t, block, nb, out, st); break;
+    default: return SAF_ERR_DTYPE;
+  }
+  return SAF_OK;
+}
+
+}  // namespace
+}  // namespace saf
+
+using namespace saf;
+
+extern "C" size_t saf_pool_topk_workspace_bytes(const saf_tensor4* q, const saf_tensor4* k,
+                                                const saf_select_cfg* cfg) {
+  if (q == nullptr || k == nullptr || cfg == nullptr || cfg->block_m <= 0 || cfg->block_n <= 0)
+    return 0;
+  const int nbq = static_cast<int>((q->S + cfg->block_m - 1) / cfg->block_m);
+  const int nbk = static_cast<int>((k->S + cfg->block_n - 1) / cfg->block_n);
+  return select_layout(q->B * q->H, nbq, nbk, static_cast<int>(q->D)).total;
+}
+
+extern "C" int32_t saf_pool_topk(const saf_tensor4* q, const saf_tensor4* k,
+                                 const saf_select_cfg* cfg, int32_t* row_ptr, int32_t* col_idx,
+                                 uint8_t* mask_out, double* score_out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (cfg == nullptr || row_ptr == nullptr || col_idx == nullptr) return SAF_ERR_ARG;
+  int32_t rc;
+  if ((rc = check_pool_operand(q)) != SAF_OK) return rc;
+  if ((rc = check_pool_operand(k)) != SAF_OK) return rc;
+  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
+  if (q->dtype != k->dtype) return SAF_ERR_DTYPE;
+  if (q->B != k->B || q->H != k->H || q->D != k->D) return SAF_ERR_SHAPE;
+  if (cfg->block_m <= 0 || cfg->block_n <= 0 || cfg->topk < 0 || cfg->text_blocks_q < 0 ||
+      cfg->text_blocks_k < 0)
+    return SAF_ERR_ARG;
+  const int64_t nbq64 = (q->S + cfg->block_m - 1) / cfg->block_m;
+  const int64_t nbk64 = (k->S + cfg->block_n - 1) / cfg->block_n;
+  if (nbk64 > 32 * kMaxM || nbq64 > 1024) return SAF_ERR_SHAPE;
+  const int64_t BH = q->B * q->H;
+  if (BH * nbq64 * nbk64 >= (int64_t(1) << 31)) return SAF_ERR_SHAPE;  // int32 CSR offsets
+  const int nbq = static_cast<int>(nbq64), nbk = static_cast<int>(nbk64);
+  const int D = static_cast<int>(q->D);
+  if (D % kDChunk != 0) return SAF_ERR_SHAPE;
+  const SelectLayout lay = select_layout(BH, nbq, nbk, D);
+  if (workspace == nullptr || workspace_bytes < lay.total) return SAF_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return SAF_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  double* qbar = reinterpret_cast<double*>(ws + lay.off_qbar);
+  double* kbar = reinterpret_cast<double*>(ws + lay.off_kbar);
+  if ((rc = pool_dispatch(q, cfg->block_m, nbq, qbar, st)) != SAF_OK) return rc;
+  if ((rc = pool_dispatch(k, cfg->block_n, nbk, kbar, st)) != SAF_OK) return rc;
+  SAF_CUDA_TRY(cudaGetLastError());
+
+  SelectArgs a{};
+  a.nbq = nbq;
+  a.nbk = nbk;
+  a.D = D;
+  a.topk = cfg->topk;
+  a.text_q = cfg->text_blocks_q;
+  a.text_k = cfg->text_blocks_k;
+  a.force_diag = cfg->force_diag;
+  a.forced_inside = cfg->forced_inside_topk;
+  a.qbar = qbar;
+  a.kbar = kbar;
+  a.padded = reinterpret_cast<int32_t*>(ws + lay.off_padded);
+  a.counts = reinterpret_cast<int32_t*>(ws + lay.off_counts);
+  a.mask_out = mask_out;
+  a.score_out = score_out;
+  const size_t smem = (static_cast<size_t>(nbk) + kRowsPerCta) * (kDChunk + 1) * sizeof(double);
+  SAF_CUDA_TRY(cudaFuncSetAttribute(score_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+  dim3 grid(static_cast<unsigned>(BH), (nbq + kRowsPerCta - 1) / kRowsPerCta);
+  score_topk_kernel<<<grid, 256, smem, st>>>(a);
+  SAF_CUDA_TRY(cudaGetLastError());
+  csr_compact_kernel<<<static_cast<unsigned>(BH), 256, 0, st>>>(nbq, nbk, a.counts, a.padded,
+                                                                row_ptr, col_idx);
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}
+
+extern "C" int32_t saf_mask_to_csr(const uint8_t* mask, int64_t BH, int32_t nbq, int32_t nbk,
+                                   int64_t stride_bh, int64_t stride_row, int32_t* row_ptr,
+                                   int32_t* col_idx, void* stream) {
+  if (mask == nullptr || row_ptr == nullptr || col_idx == nullptr) return SAF_ERR_ARG;
+  if (BH <= 0 || nbq <= 0 || nbk <= 0 || nbq > 16384) return SAF_ERR_SHAPE;
+  if (BH * static_cast<int64_t>(nbq) * nbk >= (int64_t(1) << 31)) return SAF_ERR_SHAPE;
+  if (stride_row < nbk || stride_bh < 0) return SAF_ERR_STRIDE;
+  if (BH > 2147483647) return SAF_ERR_SHAPE;
+  int32_t rc = bind_device_of(mask);
+  if (rc != SAF_OK) return rc;
+  const size_t smem = (static_cast<size_t>(nbq) + 1) * sizeof(int32_t);
+  mask_to_csr_kernel<<<static_cast<unsigned>(BH), 512, smem, static_cast<cudaStream_t>(stream)>>>(
+      mask, nbq, nbk, stride_bh, stride_row, row_ptr, col_idx);
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}

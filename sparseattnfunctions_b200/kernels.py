@@ -1,0 +1,207 @@
+"""Torch-facing wrappers of the libsaf kernels.
+
+Each function takes CUDA tensors, allocates its outputs (and workspace) with
+the PyTorch caching allocator, enqueues the kernels on the current CUDA
+stream of the tensors' device and returns without synchronising.  There is no
+CPU path: CPU tensors raise ``ValueError``.
+
+Block lists use a *segmented CSR* (see ``BlockCSR``): one CSR per head, all
+heads in one ``col_idx`` buffer with a fixed per-head segment, so it can be
+written without a device-wide prefix sum and read without a host sync.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.SAF_BF16, torch.float16: _lib.SAF_F16, torch.float32: _lib.SAF_F32}
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError("expected torch.Tensor arguments")
+        if t.device.type != "cuda":
+            raise ValueError("sparseattnfunctions_b200 kernels run on CUDA tensors only")
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def _stream_ptr(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _t4(x: torch.Tensor) -> _lib.Tensor4:
+    if x.dim() != 4:
+        raise ValueError(f"expected a [B, H, S, D] tensor, got shape {tuple(x.shape)}")
+    if x.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {x.dtype}")
+    if x.stride(-1) != 1:
+        raise ValueError("the last (D) dimension must be contiguous")
+    t = _lib.Tensor4()
+    t.data = x.data_ptr()
+    t.dtype = _DTYPES[x.dtype]
+    t.B, t.H, t.S, t.D = x.shape
+    t.stride_b, t.stride_h, t.stride_s = x.stride(0), x.stride(1), x.stride(2)
+    return t
+
+
+def _d_last(x: torch.Tensor) -> torch.Tensor:
+    return x if x.stride(-1) == 1 else x.contiguous()
+
+
+@dataclass
+class BlockCSR:
+    """Live key blocks of every query block, per head.
+
+    ``row_ptr``: int32 ``[B*H, nbq + 1]``, absolute offsets into ``col_idx``;
+    head ``g``'s entries lie in ``[g*nbq*nbk, (g+1)*nbq*nbk)``.
+    ``col_idx``: int32, capacity ``B*H*nbq*nbk``, ascending within a row.
+    """
+
+    row_ptr: torch.Tensor
+    col_idx: torch.Tensor
+    B: int
+    H: int
+    nbq: int
+    nbk: int
+    block_m: int
+    block_n: int
+    mask: Optional[torch.Tensor] = None    # uint8 [B, H, nbq, nbk] when requested
+    scores: Optional[torch.Tensor] = None  # fp64 [B, H, nbq, nbk] when requested
+
+    def nnz_per_head(self) -> torch.Tensor:
+        """Live blocks per head (device tensor, no sync)."""
+        return self.row_ptr[:, -1] - self.row_ptr[:, 0]
+
+    def to_dense(self) -> torch.Tensor:
+        """Dense bool mask ``[B, H, nbq, nbk]`` rebuilt from the CSR (torch ops;
+        for inspection and tests)."""
+        rp = self.row_ptr.long()
+        counts = (rp[:, 1:] - rp[:, :-1]).reshape(-1)
+        rows = torch.repeat_interleave(torch.arange(counts.numel(), device=rp.device), counts)
+        starts = rp[:, :-1].reshape(-1)
+        first = torch.repeat_interleave(starts, counts)
+        within = torch.arange(rows.numel(), device=rp.device) - torch.repeat_interleave(
+            torch.cumsum(counts, 0) - counts, counts)
+        cols = self.col_idx.long()[first + within]
+        dense = torch.zeros(self.B * self.H * self.nbq, self.nbk, dtype=torch.bool, device=rp.device)
+        dense[rows, cols] = True
+        return dense.view(self.B, self.H, self.nbq, self.nbk)
+
+    def live_flops(self, Sq: int, Sk: int, D: int) -> torch.Tensor:
+        """Algorithmic FLOP of the live blocks: 4*D*sum(rows_i * cols_j) with
+        the exact sizes of partial edge blocks (device tensor)."""
+        dense = self.to_dense().double()
+        rows = torch.full((self.nbq,), float(self.block_m), dtype=torch.float64, device=dense.device)
+        rows[-1] = Sq - (self.nbq - 1) * self.block_m
+        cols = torch.full((self.nbk,), float(self.block_n), dtype=torch.float64, device=dense.device)
+        cols[-1] = Sk - (self.nbk - 1) * self.block_n
+        return 4.0 * D * torch.einsum("bhij,i,j->", dense, rows, cols)
+
+
+def pool_topk(q: torch.Tensor, k: torch.Tensor, *, block_m: int, block_n: int, topk: int,
+              text_blocks_q: int = 0, text_blocks_k: int = 0, force_diag: bool = False,
+              forced_inside_topk: bool = False, return_mask: bool = False,
+              return_scores: bool = False) -> BlockCSR:
+    """Block selection by mean-pooled scores (one launch sequence, no sync).
+
+    Keeps, in every row block ``i >= text_blocks_q``, the ``topk`` columns of
+    highest ``mean(q_block_i) . mean(k_block_j)`` (fp64; ties -> lower column),
+    plus the forced columns ``j < text_blocks_k`` (and ``j == i`` with
+    ``force_diag``).  With ``forced_inside_topk`` the forced columns count
+    toward ``topk``.  Rows ``i < text_blocks_q`` are dense.
+    """
+    dev = _require_cuda(q, k)
+    q, k = _d_last(q), _d_last(k)
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    nbq, nbk = math.ceil(Sq / block_m), math.ceil(Sk / block_n)
+    cfg = _lib.SelectCfg(block_m, block_n, topk, text_blocks_q, text_blocks_k, int(force_diag),
+                         int(forced_inside_topk), 0)
+    tq, tk = _t4(q), _t4(k)
+    lib = _lib.load()
+    ws_bytes = lib.saf_pool_topk_workspace_bytes(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(cfg))
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    row_ptr = torch.empty(B * H, nbq + 1, dtype=torch.int32, device=dev)
+    col_idx = torch.empty(B * H * nbq * nbk, dtype=torch.int32, device=dev)
+    mask = torch.empty(B, H, nbq, nbk, dtype=torch.uint8, device=dev) if return_mask else None
+    scores = torch.empty(B, H, nbq, nbk, dtype=torch.float64, device=dev) if return_scores else None
+    with torch.cuda.device(dev):
+        rc = lib.saf_pool_topk(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(cfg),
+                               row_ptr.data_ptr(), col_idx.data_ptr(),
+                               mask.data_ptr() if mask is not None else None,
+                               scores.data_ptr() if scores is not None else None,
+                               ws.data_ptr(), ws.numel(), _stream_ptr(dev))
+    _lib.check("saf_pool_topk", rc)
+    return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n, mask, scores)
+
+
+def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int) -> BlockCSR:
+    """Dense boolean block mask ``[B, H, nbq, nbk]`` -> ``BlockCSR``."""
+    dev = _require_cuda(block_mask)
+    if block_mask.dim() != 4:
+        raise ValueError("block mask must be [B, H, nbq, nbk]")
+    B, H, nbq, nbk = block_mask.shape
+    m = block_mask
+    if m.dtype == torch.bool:
+        m = m.view(torch.uint8)
+    elif m.dtype != torch.uint8:
+        m = (m != 0).view(torch.uint8)
+    if m.stride(-1) != 1 or m.stride(0) != H * m.stride(1):
+        m = m.contiguous()
+    row_ptr = torch.empty(B * H, nbq + 1, dtype=torch.int32, device=dev)
+    col_idx = torch.empty(B * H * nbq * nbk, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_mask_to_csr(m.data_ptr(), B * H, nbq, nbk, m.stride(1), m.stride(2),
+                                         row_ptr.data_ptr(), col_idx.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_mask_to_csr", rc)
+    return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n)
+
+
+def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm_scale: float,
+            kv_bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Block-sparse attention over the live blocks of ``csr``.
+
+    ``kv_bias``: optional fp32 additive bias per key column, shape ``[Sk]``
+    (shared by all heads), ``[B*H, Sk]`` or ``[B, H, Sk]`` / ``[B, H, 1, Sk]``.
+    """
+    dev = _require_cuda(q, k, v)
+    q, k, v = _d_last(q), _d_last(k), _d_last(v)
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if k.shape[:2] != (B, H) or v.shape != k.shape or k.shape[3] != D:
+        raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} do not match")
+    if (csr.B, csr.H) != (B, H) or csr.nbq != math.ceil(Sq / csr.block_m) or \
+            csr.nbk != math.ceil(Sk / csr.block_n):
+        raise ValueError("block list does not match q/k shapes")
+    if out is None:
+        out = torch.empty_like(q)
+    bias_ptr, bias_stride = None, 0
+    if kv_bias is not None:
+        _require_cuda(kv_bias)
+        if kv_bias.dtype != torch.float32:
+            raise ValueError("kv_bias must be float32")
+        kb = kv_bias.reshape(-1, kv_bias.shape[-1])
+        if kb.shape[-1] != Sk or kb.shape[0] not in (1, B * H):
+            raise ValueError(f"kv_bias shape {tuple(kv_bias.shape)} does not match [B*H, Sk]")
+        kb = kb.contiguous()
+        kv_bias = kb  # keep alive for the launch
+        bias_ptr = kb.data_ptr()
+        bias_stride = 0 if kb.shape[0] == 1 else Sk
+    tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_bsa_fwd(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                                     ctypes.byref(to), csr.row_ptr.data_ptr(), csr.col_idx.data_ptr(),
+                                     csr.col_idx.numel(), csr.block_m, csr.block_n, bias_ptr,
+                                     bias_stride, float(sm_scale), _stream_ptr(dev))
+    _lib.check("saf_bsa_fwd", rc)
+    return out

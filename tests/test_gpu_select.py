@@ -1,0 +1,95 @@
+"""GPU block selection (mean-pool -> fp64 score -> top-k -> CSR) must be
+bit-exact against the oracle: same block sets, same fp64 scores, same CSR."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import selection as osel
+from sparseattnfunctions_b200 import kernels, workloads
+from sparseattnfunctions_b200.geometry import VideoGeometry
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(dev, q, k, bm, bn, topk, tq=0, tk=0, diag=False, inside=False):
+    csr = kernels.pool_topk(q.to(dev), k.to(dev), block_m=bm, block_n=bn, topk=topk,
+                            text_blocks_q=tq, text_blocks_k=tk, force_diag=diag,
+                            forced_inside_topk=inside, return_mask=True, return_scores=True)
+    torch.cuda.synchronize()
+    mask_ref, score_ref = osel.select_blocks(q, k, bm, bn, topk, tq, tk, diag, inside)
+    scores = csr.scores.cpu().numpy()
+    assert np.array_equal(scores.view(np.uint64), score_ref.view(np.uint64)), \
+        f"scores differ (max abs {np.abs(scores - score_ref).max():.3e})"
+    mask = csr.mask.cpu().numpy().astype(bool)
+    assert np.array_equal(mask, mask_ref), f"{(mask != mask_ref).sum()} mask bits differ"
+    rp_ref, ci_ref = osel.dense_to_csr(mask_ref)
+    rp = csr.row_ptr.cpu().numpy()
+    ci = csr.col_idx.cpu().numpy()
+    assert np.array_equal(rp, rp_ref)
+    for g in range(rp.shape[0]):
+        s, e = rp[g, 0], rp[g, -1]
+        assert np.array_equal(ci[s:e], ci_ref[s:e])
+    return csr
+
+
+def test_config1_selection(cuda_device):
+    """fp32, 64x64 blocks, k = ceil(0.25*32) = 8 per row,
+    diagonal forced inside the 8."""
+    q, k, _ = workloads.config1_qkv()
+    csr = _check(cuda_device, q, k, 64, 64, 8, diag=True, inside=True)
+    counts = (csr.row_ptr[:, 1:] - csr.row_ptr[:, :-1]).cpu()
+    assert torch.all(counts == 8)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_small_video_selection(cuda_device, dtype):
+    geo = VideoGeometry(26, 3, 6, 10)  # 206 tokens
+    q, k, _ = workloads.video_qkv(geo, B=2, H=3, dtype=dtype, seed=2)
+    _check(cuda_device, q, k, 64, 64, 2, tq=1, tk=1)
+
+
+def test_ragged_rectangular_selection(cuda_device):
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(1, 4, 1000, 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, 4, 1500, 64, generator=g).to(torch.bfloat16)
+    _check(cuda_device, q, k, 128, 128, 3, tq=1, tk=2)
+
+
+def test_ties_prefer_lower_column(cuda_device):
+    """Identical key blocks give identical scores; lower columns must win."""
+    k = torch.ones(1, 1, 1024, 64, dtype=torch.bfloat16)
+    q = torch.ones(1, 1, 1024, 64, dtype=torch.bfloat16)
+    csr = _check(cuda_device, q, k, 128, 128, 3)
+    dense = csr.to_dense()[0, 0].cpu()
+    assert torch.equal(dense[:, :3], torch.ones(8, 3, dtype=torch.bool))
+    assert not dense[:, 3:].any()
+
+
+def test_topk_at_least_nbk(cuda_device):
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(1, 2, 500, 64, generator=g).to(torch.bfloat16)
+    _check(cuda_device, q, q, 128, 128, 10)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_head_dims(cuda_device, d):
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(1, 2, 640, d, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, 2, 640, d, generator=g).to(torch.bfloat16)
+    _check(cuda_device, q, k, 64, 64, 3, tq=1, tk=1)
+
+
+def test_cogvideox_config2_selection(cuda_device):
+    """BASELINE config 2 at full size: S = 17776, 128-blocks, 10% -> k = 14,
+    text rows / columns (2 blocks) dense.  Bit-exact against the oracle."""
+    from sparseattnfunctions_b200.geometry import COGVIDEOX_2B as geo
+
+    q, k, _ = workloads.video_qkv(geo, B=2, H=30)
+    nb = geo.num_blocks(128)
+    topk = math.ceil(0.10 * nb)
+    csr = _check(cuda_device, q, k, 128, 128, topk, tq=geo.text_blocks(128),
+                 tk=geo.text_blocks(128))
+    nnz = csr.nnz_per_head().cpu()
+    assert int(nnz.max()) <= 2 * nb + (nb - 2) * (topk + 2)

@@ -1,0 +1,429 @@
+#!/usr/bin/env python3
+"""Benchmark of the sparse-attention hot path on B200.
+
+Default workload: one CogVideoX-2B attention layer,
+B=2, H=30, S=17776 (226 text + 13x30x45 video), D=64, bf16, 128x128 blocks,
+top-10% blocks by mean-pooled score (k = 14 of 139) with text rows/columns
+dense.  One step = block selection (mean-pool -> fp64 score -> top-k -> CSR)
++ block-sparse attention over the live blocks, inputs resident in HBM.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+N > 1 runs under torchrun, one rank per GPU; every rank processes its own
+layer (weak scaling: heads of N layers partitioned 30 per GPU, no
+collective on the data path).  Times are CUDA-event times on the launching
+stream, max over ranks.  q/k/v/o are 136 MB each (larger than the 126 MB
+L2), so no L2 flush is needed between steps.
+
+Rank 0 prints ONE JSON line (see the keys below).  ``--impl reference``
+times the reference's PyTorch masked-attention path (query-chunked boolean
+mask SDPA, restated in ``oracle/attention.py``) on the host CPU cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "ms per attention layer & effective TFLOP/s at S=17776,H=30,D=64, 10% blocks; ms/merge"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/<name>.md
+    (a line `traffic_bytes_per_launch: N`), or None."""
+    p = ROOT / "profiles" / f"{name}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_uuid: str):
+        self.samples = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", gpu_uuid, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float):
+        rows = []
+        for ts, line in self.samples:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            rows.append((ts, parts))
+        win = [r for r in rows if t0 <= r[0] <= t1]
+        if len(win) < 3:
+            win = rows
+        if not win:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(p[0]) for _, p in win if num(p[0]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, p in win for i in range(4) if p[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": num(win[0][1][1]), "reasons": reasons, "samples": len(win),
+                "power_w_max": max((num(p[2]) or 0.0) for _, p in win)}
+
+
+def init_dist():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def allreduce(x: float, op: str, world: int):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# --------------------------------------------------------------------------- workloads
+
+def c2_setup(device, rank):
+    import torch
+
+    from sparseattnfunctions_b200 import workloads
+    from sparseattnfunctions_b200.geometry import COGVIDEOX_2B as geo
+
+    B, H, D, bs, density = 2, 30, 64, 128, 0.10
+    q, k, v = workloads.video_qkv(geo, B=B, H=H, D=D, dtype=torch.bfloat16, seed=1234 + 17 * rank)
+    nb = geo.num_blocks(bs)
+    cfg = dict(B=B, H=H, S=geo.seq_len, D=D, block=bs, density=density, topk=math.ceil(density * nb),
+               text_blocks=geo.text_blocks(bs), geo=geo)
+    return (q, k, v), cfg
+
+
+def cpu_masked_baseline(qkv_cpu, mask_cpu, cfg, budget_s=12.0, threads=None):
+    """Times the reference's PyTorch masked path (oracle restatement) on the
+    host CPU over whole heads until ``budget_s`` elapses; returns
+    (TFLOP/s on the live-block FLOP of the heads done, heads done, seconds)."""
+    import torch
+
+    from oracle import attention as oatt
+
+    if threads:
+        torch.set_num_threads(threads)
+    q, k, v = qkv_cpu
+    B, H, S, D = q.shape
+    bs = cfg["block"]
+    rows = torch.full((mask_cpu.shape[2],), float(bs), dtype=torch.float64)
+    rows[-1] = S - (mask_cpu.shape[2] - 1) * bs
+    cols = torch.full((mask_cpu.shape[3],), float(bs), dtype=torch.float64)
+    cols[-1] = S - (mask_cpu.shape[3] - 1) * bs
+    flops, done = 0.0, 0
+    t0 = time.perf_counter()
+    for g in range(B * H):
+        b, h = divmod(g, H)
+        oatt.masked_sdpa_cpu(q, k, v, mask_cpu, 1.0 / math.sqrt(D), bs, bs, q_chunk=2048, heads=[g])
+        flops += float(4.0 * D * torch.einsum("ij,i,j->", mask_cpu[b, h].double(), rows, cols))
+        done += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return flops / dt / 1e12, done, dt
+
+
+# --------------------------------------------------------------------------- arms
+
+def run_saf(args, world, rank, local):
+    import torch
+
+    from sparseattnfunctions_b200 import kernels
+    from sparseattnfunctions_b200.special_attentions.block_mask_attn import BlockSparseAttention
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    (q_c, k_c, v_c), cfg = c2_setup(dev, rank)
+    q, k, v = q_c.to(dev), k_c.to(dev), v_c.to(dev)
+    out = torch.empty_like(q)
+    bs, D = cfg["block"], cfg["D"]
+    scale = 1.0 / math.sqrt(D)
+    sel_kw = dict(block_m=bs, block_n=bs, topk=cfg["topk"], text_blocks_q=cfg["text_blocks"],
+                  text_blocks_k=cfg["text_blocks"])
+
+    def step():
+        csr = kernels.pool_topk(q, k, **sel_kw)
+        kernels.bsa_fwd(q, k, v, csr, scale, out=out)
+        return csr
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        csr = step()
+    torch.cuda.synchronize()
+    live_flops = float(csr.live_flops(cfg["S"], cfg["S"], D))
+    dense_flops = 4.0 * cfg["B"] * cfg["H"] * cfg["S"] ** 2 * D
+    nnz = int(csr.nnz_per_head().sum())
+    launches_per_step = 5  # pool q, pool k, score+top-k, CSR compaction, attention
+
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    sampler = ClockSampler(uuid)
+    time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    w0 = time.time()
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        csr = kernels.pool_topk(q, k, **sel_kw)
+        ev[i][1].record(stream)
+        kernels.bsa_fwd(q, k, v, csr, scale, out=out)
+        ev[i][2].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    w1 = time.time()
+    barrier(world)
+    sampler.stop()
+    elapsed = t_start.elapsed_time(t_end)
+    sel_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    att_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    max_elapsed = allreduce(elapsed, "max", world)
+    total_flops = allreduce(live_flops, "sum", world)
+    ms_per_step = max_elapsed / args.steps
+    value = total_flops / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the public processor, host buffers
+    proc = BlockSparseAttention(block_size=bs, density=cfg["density"], geometry=cfg["geo"])
+    hq, hk, hv = (t.pin_memory() for t in (q_c, k_c, v_c))
+    ho = torch.empty_like(hq).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        o = proc(dq, dk, dv)
+        ho.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = allreduce(e0.elapsed_time(e1), "max", world) / e2e_steps
+    e2e_val = total_flops / (e2e_ms * 1e-3) / 1e12
+    h2d = 3 * q.numel() * q.element_size()
+    d2h = out.numel() * out.element_size()
+    ok_e2e = torch.equal(ho, out.cpu())
+
+    # ---- roofline of the dominant kernel (attention) and of the selection pass
+    peaks, peak_kind = load_peaks()
+    att_tflops = live_flops / (att_ms * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    sel_bytes = 2 * q.numel() * q.element_size()
+    sel_gbs = sel_bytes / (sel_ms * 1e-3) / 1e9
+    traffic = profile_traffic("bsa_fwd_sm100_c2")
+    clocks = sampler.summary(w0, w1)
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded smooth field + noise, CogVideoX-2B shapes)",
+            "config": {"workload": "config2: CogVideoX-2B attention layer, select + block-sparse attention",
+                       "B": cfg["B"], "H": cfg["H"], "S": cfg["S"], "D": D, "block": bs,
+                       "density": cfg["density"], "topk": cfg["topk"],
+                       "text_blocks_dense": cfg["text_blocks"], "live_blocks_per_layer": nnz,
+                       "live_fraction": round(nnz / (cfg["B"] * cfg["H"] * csr.nbq * csr.nbk), 4),
+                       "live_tflop_per_layer": round(live_flops / 1e12, 4),
+                       "l2": "inputs larger than L2 (q/k/v/o 136 MB each), no flush",
+                       "parallelism": f"{world} independent layers, 30 heads per GPU"},
+            "ms_per_layer": round(ms_per_step, 4),
+            "dense_equiv_tflops": round(dense_flops * world / (ms_per_step * 1e-3) / 1e12, 1),
+            "kernels_ms": {"select": round(sel_ms, 4), "attention": round(att_ms, 4)},
+            "select_hbm": {"bytes": sel_bytes, "gbs": round(sel_gbs, 1),
+                           "frac": round(sel_gbs / peaks["hbm_gbs"], 3)},
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_val, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps,
+                    "api": "special_attentions.block_mask_attn.BlockSparseAttention.__call__",
+                    "matches_device_result": ok_e2e},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "bsa_fwd_sm100_kernel<128,false,true>",
+                         "achieved": round(att_tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(att_tflops / peak, 3),
+                         "frac_sustained": round(att_tflops / peaks.get("bf16_tflops_sustained", peak), 3),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops burst)",
+                         "traffic": traffic,
+                         "algorithmic_flop_per_launch": live_flops},
+        }
+    return line, (q_c, k_c, v_c), csr, cfg
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference's PyTorch masked path on the host CPU."""
+    import torch
+
+    if rank != 0:
+        return None
+    from oracle import selection as osel
+
+    (q, k, v), cfg = c2_setup("cpu", 0)
+    bs = cfg["block"]
+    mask, _ = osel.select_blocks(q, k, bs, bs, cfg["topk"], cfg["text_blocks"], cfg["text_blocks"])
+    mask = torch.from_numpy(mask)
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    heads_per_step = max(1, args.ref_heads)
+    vals = []
+    t_all = 0.0
+    for i in range(args.warmup + args.steps):
+        g0 = (i * heads_per_step) % (cfg["B"] * cfg["H"])
+        sub = [g0 + j for j in range(heads_per_step) if g0 + j < cfg["B"] * cfg["H"]]
+        qs, ks, vs_ = q, k, v
+        t0 = time.perf_counter()
+        from oracle import attention as oatt
+        oatt.masked_sdpa_cpu(qs, ks, vs_, mask, 1.0 / math.sqrt(cfg["D"]), bs, bs, q_chunk=2048,
+                             heads=sub)
+        dt = time.perf_counter() - t0
+        rows = torch.full((mask.shape[2],), float(bs), dtype=torch.float64)
+        rows[-1] = cfg["S"] - (mask.shape[2] - 1) * bs
+        fl = sum(float(4.0 * cfg["D"] * torch.einsum("ij,i,j->", mask[g // cfg["H"], g % cfg["H"]].double(),
+                                                     rows, rows)) for g in sub)
+        if i >= args.warmup:
+            vals.append(fl / dt / 1e12)
+            t_all += dt
+    value = statistics.median(vals)
+    sample = f"{heads_per_step} of 60 (b,h) heads per step, query chunks of 2048, bf16 masked SDPA"
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * t_all / max(1, args.steps), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded smooth field + noise, CogVideoX-2B shapes)",
+        "config": {"workload": "config2: CogVideoX-2B attention layer (reference masked path, CPU)",
+                   "B": cfg["B"], "H": cfg["H"], "S": cfg["S"], "D": cfg["D"], "block": bs,
+                   "density": cfg["density"], "topk": cfg["topk"]},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["saf", "reference"], default="saf")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--ref-heads", type=int, default=1, help="heads per step of the reference arm")
+    ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world, rank, local = init_dist() if args.impl == "saf" else (
+        int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    line, qkv_cpu, csr, cfg = run_saf(args, world, rank, local)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        mask_cpu = csr.to_dense().cpu()
+        val, heads, secs = cpu_masked_baseline(qkv_cpu, mask_cpu, cfg, budget_s=args.cpu_budget)
+        import torch
+        line["cpu_baseline"] = {"value": round(val, 5), "unit": UNIT, "cores": torch.get_num_threads(),
+                                "kind": "port",
+                                "sample": f"{heads} of 60 (b,h) heads of config 2 in {secs:.1f} s: "
+                                          "query-chunked (2048) bf16 masked SDPA, same block mask"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

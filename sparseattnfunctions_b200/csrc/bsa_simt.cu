@@ -263,9 +263,9 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
   if (block_m <= 0 || block_n <= 0) return SAF_ERR_ARG;
   if (kv_bias_stride_bh < 0) return SAF_ERR_STRIDE;
   if (q->S > 0x7fffffff || k->S > 0x7fffffff || q->B * q->H > 65535) return SAF_ERR_SHAPE;
-  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (q->dtype == SAF_F32) {
+    if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
     return bsa_fwd_simt(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                         kv_bias_stride_bh, sm_scale, st);
   }
@@ -279,6 +279,7 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
         (t->stride_b * 2) % 16 != 0)
       return SAF_ERR_STRIDE;
   }
+  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
   return bsa_fwd_sm100(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                        kv_bias_stride_bh, sm_scale, st);
 }

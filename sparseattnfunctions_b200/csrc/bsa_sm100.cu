@@ -18,12 +18,16 @@
 //   warp 1      TMEM allocator and single-thread tcgen05.mma issuer:
 //               S = Q K^T (SS form) into TMEM, then O += P V (TS form, P read
 //               from TMEM) for the previous block.
-//   warps 2..5  softmax: one thread per query row (= TMEM lane).  Reads S
-//               from TMEM twice (row max, then exp2 per 32-column chunk, so
-//               only 32 scores are live in registers), keeps the running max
-//               m and sum l in registers, writes P (bf16/f16 pairs) into TMEM
-//               and rescales the O accumulator in TMEM only when a row's max
-//               grows by more than 2^8 (so P <= 256; exact after 1/l).
+//   warps 2,3   idle (they complete warpgroup 0 for the register split).
+//   warps 4..11 softmax: two threads per query row (TMEM lane); warps 4-7
+//               take key columns [0, BN/2), warps 8-11 [BN/2, BN).  Each
+//               thread reads its half-row of S once into registers (so the
+//               next QK^T may start at once), the pair exchanges its row max
+//               through shared memory (an mbarrier, not a named barrier, so
+//               the wait keeps its time budget), and each writes its half of
+//               P (bf16/f16 pairs) into TMEM.  The running max only moves when
+//               it grows by more than 2^8 (lazy rescale: P <= 256, exact
+//               after the final 1/l); O in TMEM is rescaled only then.
 // TMEM columns: S [0,128) | O [128,192) | P [192,256).
 //
 // Every mbarrier wait has a time budget; on expiry the CTA raises a shared
@@ -38,7 +42,12 @@ constexpr int kBM = 128;       // query rows per CTA
 constexpr int kD = 64;         // head dim handled by this kernel
 constexpr int kKS = 3;         // K stages
 constexpr int kVS = 2;         // V stages
-constexpr int kThreads = 192;  // 6 warps
+constexpr int kThreads = 384;  // 12 warps = 3 warpgroups
+// Register split: launched at 80 per thread (2 CTAs x 384 threads per SM);
+// warpgroup 0 (producer, MMA issuer, 2 idle warps) drops to 32, the two
+// softmax warpgroups rise to 104: 128*32 + 256*104 = 30720 = 384*80.
+constexpr uint32_t kRegsCtl = 32, kRegsSoftmax = 104;
+static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= kThreads * 80, "register split");
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128, kColP = 192;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -67,7 +76,7 @@ struct BsaParams {
 // all of them see the same sequence.  Out-of-range columns are skipped.
 struct TileIter {
   const int32_t* cols;
-  int64_t p0, e0, p1, e1;
+  int32_t p0, e0, p1, e1;  // CSR offsets are int32 by contract
   int nbk;
   bool two_rows;
   unsigned int* status;
@@ -77,8 +86,8 @@ struct TileIter {
     nbk = p.nbk;
     status = p.status;
     const int32_t* rp = p.row_ptr + static_cast<int64_t>(g) * (p.nbq + 1);
-    auto clampi = [&](int64_t x) {
-      return x < 0 ? int64_t(0) : (x > p.col_capacity ? p.col_capacity : x);
+    auto clampi = [&](int32_t x) -> int32_t {
+      return x < 0 ? 0 : (static_cast<int64_t>(x) > p.col_capacity ? static_cast<int32_t>(p.col_capacity) : x);
     };
     two_rows = (p.bm == 64);
     const int r0 = two_rows ? 2 * tile : tile;
@@ -138,10 +147,13 @@ struct Layout {
   static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + kKS * kKVBytes;
   static constexpr int kOffBias = kOffV + kVS * kKVBytes;
-  static constexpr int kOffBar = kOffBias + kVS * BN * 4;
+  static constexpr int kOffXm = kOffBias + kVS * BN * 4;   // [2 parity][2 half][128] row max
+  static constexpr int kOffXl = kOffXm + 2 * 2 * kBM * 4;    // [2 half][128] row sum
+  static constexpr int kOffBar = kOffXl + 2 * kBM * 4;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain
-  static constexpr int kNumBars = 1 + 2 * kKS + 3 * kVS + 5;
+  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain,
+  //           x_full[2], x_end
+  static constexpr int kNumBars = 1 + 2 * kKS + 3 * kVS + 8;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
@@ -180,6 +192,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_p_full = bar_s_full + 16;
   const uint32_t bar_pv_full = bar_s_full + 24;
   const uint32_t bar_drain = bar_s_full + 32;
+  auto bar_x_full = [&](int par) { return bar_s_full + 40u + 8u * par; };
+  const uint32_t bar_x_end = bar_s_full + 56;
+  float* xm = reinterpret_cast<float*>(smem + L::kOffXm);
+  float* xl = reinterpret_cast<float*>(smem + L::kOffXl);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
 
@@ -195,10 +211,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar_b_full(s), 32);
     }
     mbar_init(bar_s_full, 1);
-    mbar_init(bar_s_empty, 128);
-    mbar_init(bar_p_full, 128);
+    mbar_init(bar_s_empty, 256);
+    mbar_init(bar_p_full, 256);
     mbar_init(bar_pv_full, 1);
     mbar_init(bar_drain, 1);
+    mbar_init(bar_x_full(0), 256);
+    mbar_init(bar_x_full(1), 256);
+    mbar_init(bar_x_end, 256);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -213,8 +232,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
+  // Roles.  No code is shared after the register split: each warpgroup
+  // ends with its own copy of the teardown (named barrier 1 over all
+  // threads, then warp 1 frees TMEM).
+  if (warp < 4) {
+    setmaxnreg_dec<kRegsCtl>();
+    if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       mbar_arrive_expect_tx(bar_q, L::kQBytes);
@@ -266,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+    } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdescQK = idesc_f16(kBM, BN, kBF16, false, false);
@@ -326,16 +349,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_commit(bar_drain);
       mbar_drain(bar_drain, 0, p.status);
     }
+    }
+    // ------------------------------------------------------------ teardown
+    __syncwarp();
+    tc_fence_before();
+    named_barrier_sync(1, kThreads);
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, kTmemCols);
+    }
   } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax
+    constexpr int HC = BN / 2;  // key columns per thread
     const int quarter = warp & 3;
+    const int chalf = (warp - 4) >> 2;  // column half of this warp
     const int row = quarter * 32 + lane;
-    const uint32_t half = static_cast<uint32_t>(row >> 6);
+    const uint32_t rhalf = static_cast<uint32_t>(row >> 6);  // row half (64-row mask blocks)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_addr + kColS;
-    const uint32_t tO = tmem + lane_addr + kColO;
-    const uint32_t tP = tmem + lane_addr + kColP;
+    const uint32_t tS = tmem + lane_addr + kColS + chalf * HC;
+    const uint32_t tO = tmem + lane_addr + kColO + chalf * (kD / 2);
+    const uint32_t tP = tmem + lane_addr + kColP + chalf * (HC / 2);
     const float sl2 = p.scale_log2;
+    const f2 sl2x2 = mk2(sl2, sl2);
 
     float m_run = -INFINITY, l_run = 0.f;
     TileIter it;
@@ -350,44 +386,67 @@ __global__ void __launch_bounds__(kThreads, 2)
         break;
       }
       tc_fence_after();
-      const bool live = (rm >> half) & 1u;
-      const int valid = p.Sk - col * BN;
-      const float* bb = sBias + (j % kVS) * BN;
+      // Two x32 loads (not one x64: no single instruction may need more
+      // registers than the launch budget).
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tS, r0);
+      if constexpr (HC == 64) tmem_ld32(tS + 32, r1);
+      tmem_wait_ld(r0);
+      if constexpr (HC == 64) tmem_wait_ld(r1);
+      auto r = [&](int e) -> uint32_t { return e < 32 ? r0[e] : r1[e - 32]; };
+      // This thread's half of S is in registers: the next QK^T may overwrite S.
+      tc_fence_before();
+      mbar_arrive(bar_s_empty);
+
+      const bool live = (rm >> rhalf) & 1u;
+      const int valid = p.Sk - col * BN - chalf * HC;  // valid columns of this half
+      const bool fast = live && valid >= HC;             // warp-uniform
+      float t[HC];
       if constexpr (kBias) {
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_b_full(j % kVS), (j / kVS) & 1, abort_flag,
+        const int sv = j % kVS;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_b_full(sv), (j / kVS) & 1, abort_flag,
                                                 p.status, p.budget_ns))) {
           ok = false;
           break;
         }
-      }
-      // Loads 32 scores of chunk c as log2-domain logits (bias added when
-      // present, otherwise still unscaled) with masked entries = -inf.
-      auto load_chunk = [&](int c, float (&t)[32]) {
-        uint32_t r[32];
-        tmem_ld32(tS + c * 32, r);
-        tmem_wait_ld(r);
+        const float* bb = sBias + sv * BN + chalf * HC;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int cc = c * 32 + e;
-          float x = __uint_as_float(r[e]);
-          if constexpr (kBias) x = fmaf(x, sl2, bb[cc]);
-          t[e] = (live && cc < valid) ? x : -INFINITY;
+        for (int e = 0; e < HC; e += 2) {
+          const float2 bv = *reinterpret_cast<const float2*>(bb + e);
+          const f2 x = fma2(mk2(__uint_as_float(r(e)), __uint_as_float(r(e + 1))), sl2x2,
+                            mk2(bv.x, bv.y));
+          t[e] = lo2(x);
+          t[e + 1] = hi2(x);
         }
-      };
-
-      // Pass 1: row max.
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32];
-        load_chunk(c, t);
+      } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, t[e]);
-        // Keep each chunk's reduction ahead of the next TMEM load (bounds the
-        // number of live scores to one chunk).
-        asm volatile("" : "+f"(mx));
+        for (int e = 0; e < HC; ++e) t[e] = __uint_as_float(r(e));
       }
-      const float m_cand = kBias ? mx : mx * sl2;
+      if (!fast) {
+#pragma unroll
+        for (int e = 0; e < HC; ++e)
+          if (!(live && e < valid)) t[e] = -INFINITY;
+      }
+      // Local max of this half row: four running 3-input-max accumulators
+      // (no temporary array next to the live scores).
+      float mx;
+      {
+        float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < HC / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
+        mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
+      }
+      if constexpr (!kBias) mx *= sl2;
+      // Exchange the half-row maxima of the pair (parity-buffered).
+      float* xbuf = xm + (j & 1) * 2 * kBM;
+      xbuf[chalf * kBM + row] = mx;
+      mbar_arrive(bar_x_full(j & 1));
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_x_full(j & 1), (j >> 1) & 1, abort_flag,
+                                              p.status, p.budget_ns))) {
+        ok = false;
+        break;
+      }
+      const float m_cand = fmaxf(mx, xbuf[(chalf ^ 1) * kBM + row]);
       const bool upd = m_cand > m_run + kRescaleThreshold;
       const float m_new = upd ? m_cand : m_run;
       const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
@@ -403,49 +462,39 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc_fence_after();
         if (__any_sync(0xffffffffu, upd)) {
+          uint32_t orr[32];
+          tmem_ld32(tO, orr);
+          tmem_wait_ld(orr);
 #pragma unroll
-          for (int c = 0; c < kD / 32; ++c) {
-            uint32_t orr[32];
-            tmem_ld32(tO + c * 32, orr);
-            tmem_wait_ld(orr);
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-            tmem_st32(tO + c * 32, orr);
-          }
+          for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+          tmem_st32(tO, orr);
         }
       }
 
-      // Pass 2: P = exp2(logit - m) in the input type, row sum in fp32.
-      float rs0 = 0.f, rs1 = 0.f;
-// Not unrolled: keeps the next chunk's TMEM load from being hoisted over
-      // this chunk's exp2 work (which would hold 2 chunks in registers).
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float t[32];
-        load_chunk(c, t);
+      // P = exp2(logit - m) in the input type; row sum in fp32 pairs.  Done
+      // 32 scores at a time; the empty asm after each store keeps the next
+      // part's exp2 from being scheduled early (bounds live registers).
+      const f2 negm2 = mk2(neg_m, neg_m);
+      f2 rs = mk2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < HC / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float e0, e1;
-          if constexpr (kBias) {
-            e0 = ex2_approx(t[2 * e] + neg_m);
-            e1 = ex2_approx(t[2 * e + 1] + neg_m);
-          } else {
-            e0 = ex2_approx(fmaf(t[2 * e], sl2, neg_m));
-            e1 = ex2_approx(fmaf(t[2 * e + 1], sl2, neg_m));
-          }
-          rs0 += e0;
-          rs1 += e1;
+          f2 x = mk2(t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
+          x = kBias ? add2(x, negm2) : fma2(x, sl2x2, negm2);
+          const float e0 = ex2_approx(lo2(x)), e1 = ex2_approx(hi2(x));
+          rs = add2(rs, mk2(e0, e1));
           pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
         }
         tmem_st16(tP + c * 16, pk);
-        asm volatile("" : "+f"(rs0), "+f"(rs1));
+        if (c + 1 < HC / 32) {
+          asm volatile("" : "+l"(rs.v));
+#pragma unroll
+          for (int e = 0; e < 32; ++e) asm volatile("" : "+f"(t[(c + 1) * 32 + e]));
+        }
       }
-      // S has been read for the last time: the next QK^T may overwrite it.
-      tc_fence_before();
-      mbar_arrive(bar_s_empty);
-      l_run = l_run * alpha + (rs0 + rs1);
+      l_run = l_run * alpha + (lo2(rs) + hi2(rs));
       m_run = m_new;
       tmem_wait_st();
       tc_fence_before();
@@ -454,54 +503,50 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---------------------------------------------------------- epilogue
-    // O is read back 32 columns at a time, normalised by 1/l and stored.
-    // A zero row sum gives 0 * inf = NaN, matching the reference; a tile with
-    // no live block never wrote O and stores 0 * inf = NaN as well.
+    // Row sum = sum of the pair's partial sums.  O is read back 32 columns per
+    // thread, normalised by 1/l and stored.  A zero row sum gives
+    // 0 * inf = NaN, matching the reference; a tile with no live block never
+    // wrote O and stores NaN as well.
     const bool have_o =
         ok && j > 0 &&
         __all_sync(0xffffffffu,
                    mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status, p.budget_ns));
     if (have_o) tc_fence_after();
+    xl[chalf * kBM + row] = l_run;
+    mbar_arrive(bar_x_end);
+    const bool have_l = ok && __all_sync(0xffffffffu, mbar_wait(bar_x_end, 0, abort_flag, p.status,
+                                                                 p.budget_ns));
+    const float l_tot = l_run + (have_l ? xl[(chalf ^ 1) * kBM + row] : 0.f);
     const int qrow = q0 + row;
-    const float inv_l = 1.f / l_run;
+    const float inv_l = 1.f / l_tot;
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
                    2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
-                        static_cast<int64_t>(qrow) * p.o_ss);
-    const bool write = (j == 0 || have_o) && !*abort_flag && qrow < p.Sq;
+                        static_cast<int64_t>(qrow) * p.o_ss + chalf * (kD / 2));
+    const bool write = (j == 0 || have_o) && have_l && !*abort_flag && qrow < p.Sq;
+    uint32_t orr[32];
+    if (have_o) {
+      tmem_ld32(tO, orr);
+      tmem_wait_ld(orr);
+    } else {
 #pragma unroll
-    for (int c = 0; c < kD / 32; ++c) {
-      uint32_t orr[32];
-      if (have_o) {
-        tmem_ld32(tO + c * 32, orr);
-        tmem_wait_ld(orr);
-      } else {
+      for (int e = 0; e < 32; ++e) orr[e] = 0u;
+    }
+    if (write) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) orr[e] = 0u;
-      }
-      if (write) {
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          uint4 w;
-          uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float lo = __uint_as_float(orr[v * 8 + 2 * e]) * inv_l;
-            const float hi = __uint_as_float(orr[v * 8 + 2 * e + 1]) * inv_l;
-            pw[e] = kBF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
-          }
-          reinterpret_cast<uint4*>(dst)[c * 4 + v] = w;
+        for (int e = 0; e < 4; ++e) {
+          const float lo = __uint_as_float(orr[v * 8 + 2 * e]) * inv_l;
+          const float hi = __uint_as_float(orr[v * 8 + 2 * e + 1]) * inv_l;
+          pw[e] = kBF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
         }
+        reinterpret_cast<uint4*>(dst)[v] = w;
       }
     }
-  }
-
-  // ---------------------------------------------------------------- teardown
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tc_fence_before();
+    named_barrier_sync(1, kThreads);
   }
 }
 

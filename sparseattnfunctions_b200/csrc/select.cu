@@ -28,7 +28,6 @@ namespace {
 
 constexpr int kPoolThreads = 256;
 constexpr int kMaxM = 16;  // column slots per lane: nbk <= 512
-constexpr int kRowsPerCta = 16;
 constexpr int kDChunk = 32;
 
 __device__ __forceinline__ double to_f64(__nv_bfloat16 x) {
@@ -37,33 +36,55 @@ __device__ __forceinline__ double to_f64(__nv_bfloat16 x) {
 __device__ __forceinline__ double to_f64(__half x) { return static_cast<double>(__half2float(x)); }
 __device__ __forceinline__ double to_f64(float x) { return static_cast<double>(x); }
 
-// grid (nb, B*H); mean over the rows of one block, fp64.
-template <typename T>
-__global__ void __launch_bounds__(kPoolThreads) pool_mean_kernel(
-    const T* __restrict__ x, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int block,
-    double* __restrict__ out) {
+struct PoolOperand {
+  const void* x;
+  int S;
+  int64_t sb, sh, ss;
+  int block, nb;
+  double* out;  // [B*H, nb, D]
+};
+
+// grid (max nb, B*H, 2): z = 0 pools q, z = 1 pools k.  Mean over the rows of
+// one block in fp64.  Each thread owns one 16-byte column chunk and issues all
+// of its row loads before accumulating, so a CTA keeps the whole block in
+// flight.
+template <typename T, int kMaxRowsPerThread>
+__global__ void __launch_bounds__(kPoolThreads) pool_mean_kernel(PoolOperand q_op,
+                                                                 PoolOperand k_op, int H, int D) {
   constexpr int VEC = 16 / sizeof(T);
   extern __shared__ double part[];  // [groups][D]
+  const PoolOperand& op = blockIdx.z == 0 ? q_op : k_op;
   const int blk = blockIdx.x, g = blockIdx.y;
+  if (blk >= op.nb) return;
   const int b = g / H, h = g % H;
-  const int r0 = blk * block;
-  const int nrows = min(block, S - r0);
-  const int vpr = D / VEC;                 // vectors per row
-  const int groups = kPoolThreads / vpr;   // rows processed in parallel
+  const int r0 = blk * op.block;
+  const int nrows = min(op.block, op.S - r0);
+  const int vpr = D / VEC;                // vectors per row
+  const int groups = kPoolThreads / vpr;  // rows processed in parallel
   const int tid = threadIdx.x;
   const int vc = tid % vpr, rg = tid / vpr;
-  const T* base = x + static_cast<int64_t>(b) * sb + static_cast<int64_t>(h) * sh;
+  const T* base = static_cast<const T*>(op.x) + static_cast<int64_t>(b) * op.sb +
+                  static_cast<int64_t>(h) * op.sh + static_cast<int64_t>(r0) * op.ss + vc * VEC;
   double acc[VEC];
 #pragma unroll
   for (int e = 0; e < VEC; ++e) acc[e] = 0.0;
-  if (rg < groups) {
-    for (int r = rg; r < nrows; r += groups) {
-      const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<int64_t>(r0 + r) * ss +
-                                                      vc * VEC);
-      const T* pv = reinterpret_cast<const T*>(&v);
+  // Threads past `groups` rows (D / VEC not dividing the block size) idle.
+  for (int r = rg; rg < groups && r < nrows; r += groups * kMaxRowsPerThread) {
+    uint4 v[kMaxRowsPerThread];
+#pragma unroll
+    for (int u = 0; u < kMaxRowsPerThread; ++u) {
+      const int rr = r + u * groups;
+      v[u] = rr < nrows ? __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(rr) * op.ss))
+                        : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kMaxRowsPerThread; ++u) {
+      const T* pv = reinterpret_cast<const T*>(&v[u]);
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc[e] += to_f64(pv[e]);
     }
+  }
+  if (rg < groups) {
 #pragma unroll
     for (int e = 0; e < VEC; ++e) part[rg * D + vc * VEC + e] = acc[e];
   }
@@ -71,7 +92,7 @@ __global__ void __launch_bounds__(kPoolThreads) pool_mean_kernel(
   for (int d = tid; d < D; d += kPoolThreads) {
     double s = 0.0;
     for (int k = 0; k < groups; ++k) s += part[k * D + d];
-    out[(static_cast<int64_t>(g) * gridDim.x + blk) * D + d] = s / static_cast<double>(nrows);
+    op.out[(static_cast<int64_t>(g) * op.nb + blk) * D + d] = s / static_cast<double>(nrows);
   }
 }
 
@@ -90,21 +111,21 @@ __device__ __forceinline__ bool better(double a, int ia, double b, int ib) {
   return a > b || (a == b && ia < ib);
 }
 
-// grid (B*H, ceil(nbq / kRowsPerCta)), 256 threads; one warp per row.
+// grid (B*H, ceil(nbq / 8)), 256 threads; one warp per row block.  The key
+// means of the head are staged in shared memory 32 dims at a time; every lane
+// owns columns lane + 32m (m < M) and accumulates their fp64 scores with d
+// ascending.  The top-k is k rounds of a warp arg-max (ties -> lower column).
+template <int M>
 __global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
-  extern __shared__ double ks[];  // [nbk][kDChunk+1] then [kRowsPerCta][kDChunk+1]
+  extern __shared__ double ks[];  // [nbk][kDChunk+1] then [8][kDChunk+1]
   double* qs = ks + a.nbk * (kDChunk + 1);
   const int g = blockIdx.x;
-  const int row_base = blockIdx.y * kRowsPerCta;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int M = (a.nbk + 31) / 32;
-  constexpr int kRowsPerWarp = kRowsPerCta / 8;
+  const int row = blockIdx.y * 8 + warp;
 
-  double sc[kRowsPerWarp][kMaxM];
+  double sc[M];
 #pragma unroll
-  for (int rr = 0; rr < kRowsPerWarp; ++rr)
-#pragma unroll
-    for (int m = 0; m < kMaxM; ++m) sc[rr][m] = 0.0;
+  for (int m = 0; m < M; ++m) sc[m] = 0.0;
 
   const double* kb = a.kbar + static_cast<int64_t>(g) * a.nbk * a.D;
   const double* qb = a.qbar + static_cast<int64_t>(g) * a.nbq * a.D;
@@ -114,96 +135,91 @@ __global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
       const int j = idx / kDChunk, d = idx % kDChunk;
       ks[j * (kDChunk + 1) + d] = kb[static_cast<int64_t>(j) * a.D + d0 + d];
     }
-    for (int idx = threadIdx.x; idx < kRowsPerCta * kDChunk; idx += blockDim.x) {
-      const int r = idx / kDChunk, d = idx % kDChunk;
-      const int row = row_base + r;
-      qs[r * (kDChunk + 1) + d] = row < a.nbq ? qb[static_cast<int64_t>(row) * a.D + d0 + d] : 0.0;
+    {
+      const int r = threadIdx.x / kDChunk, d = threadIdx.x % kDChunk;  // 8 x 32
+      const int rr = blockIdx.y * 8 + r;
+      qs[r * (kDChunk + 1) + d] = rr < a.nbq ? qb[static_cast<int64_t>(rr) * a.D + d0 + d] : 0.0;
     }
     __syncthreads();
+    const double* qr = qs + warp * (kDChunk + 1);
 #pragma unroll
-    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-      const int r = warp * kRowsPerWarp + rr;
-#pragma unroll
-      for (int m = 0; m < kMaxM; ++m) {
-        const int j = lane + 32 * m;
-        if (m < M && j < a.nbk) {
-          double s = sc[rr][m];
-          for (int d = 0; d < kDChunk; ++d)
-            s = __dadd_rn(s, __dmul_rn(qs[r * (kDChunk + 1) + d], ks[j * (kDChunk + 1) + d]));
-          sc[rr][m] = s;
-        }
+    for (int m = 0; m < M; ++m) {
+      const int j = lane + 32 * m;
+      if (j < a.nbk) {
+        double s = sc[m];
+        const double* kr = ks + j * (kDChunk + 1);
+#pragma unroll 8
+        for (int d = 0; d < kDChunk; ++d) s = __dadd_rn(s, __dmul_rn(qr[d], kr[d]));
+        sc[m] = s;
       }
     }
   }
+  if (row >= a.nbq) return;
 
+  const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
+  uint32_t forced = 0, eligible = 0, sel = 0;  // bit m <-> column lane + 32m
+  const bool text_row = row < a.text_q;
 #pragma unroll
-  for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-    const int row = row_base + warp * kRowsPerWarp + rr;
-    if (row >= a.nbq) continue;
-    const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
-    uint32_t forced = 0, eligible = 0, sel = 0;  // bit m <-> column lane + 32m
-    int nforced = 0;
-    const bool text_row = row < a.text_q;
-#pragma unroll
-    for (int m = 0; m < kMaxM; ++m) {
-      const int j = lane + 32 * m;
-      if (m < M && j < a.nbk) {
-        const bool f = text_row || j < a.text_k || (a.force_diag && j == row);
-        if (f) forced |= 1u << m;
-        if (!(f && a.forced_inside)) eligible |= 1u << m;
-      }
+  for (int m = 0; m < M; ++m) {
+    const int j = lane + 32 * m;
+    if (j < a.nbk) {
+      const bool f = text_row || j < a.text_k || (a.force_diag && j == row);
+      if (f) forced |= 1u << m;
+      if (!(f && a.forced_inside)) eligible |= 1u << m;
     }
-#pragma unroll
-    for (int m = 0; m < kMaxM; ++m) nforced += __popc(__ballot_sync(0xffffffffu, (forced >> m) & 1u));
-    int krem = a.forced_inside ? a.topk - nforced : a.topk;
-    if (text_row) krem = 0;
-    for (int round = 0; round < krem; ++round) {
-      double best = -INFINITY;
-      int bj = 0x7fffffff;
-#pragma unroll
-      for (int m = 0; m < kMaxM; ++m) {
-        if (((eligible & ~sel) >> m) & 1u) {
-          const int j = lane + 32 * m;
-          if (better(sc[rr][m], j, best, bj)) {
-            best = sc[rr][m];
-            bj = j;
-          }
-        }
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const double ob = __shfl_xor_sync(0xffffffffu, best, off);
-        const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
-        if (better(ob, oj, best, bj)) {
-          best = ob;
-          bj = oj;
-        }
-      }
-      if (bj == 0x7fffffff) break;  // no candidate left
-      if ((bj & 31) == lane) sel |= 1u << (bj >> 5);
-    }
-    sel |= forced;
-    int base = 0;
-#pragma unroll
-    for (int m = 0; m < kMaxM; ++m) {
-      const uint32_t bal = __ballot_sync(0xffffffffu, (sel >> m) & 1u);
-      if ((sel >> m) & 1u) {
-        const int pos = base + __popc(bal & ((1u << lane) - 1u));
-        a.padded[rbase + pos] = lane + 32 * m;
-      }
-      base += __popc(bal);
-      const int j = lane + 32 * m;
-      if (m < M && j < a.nbk) {
-        if (a.mask_out) a.mask_out[rbase + j] = (sel >> m) & 1u;
-        if (a.score_out) a.score_out[rbase + j] = sc[rr][m];
-      }
-    }
-    if (lane == 0) a.counts[static_cast<int64_t>(g) * a.nbq + row] = base;
   }
+  int nforced = 0;
+#pragma unroll
+  for (int m = 0; m < M; ++m) nforced += __popc(__ballot_sync(0xffffffffu, (forced >> m) & 1u));
+  int krem = a.forced_inside ? a.topk - nforced : a.topk;
+  if (text_row) krem = 0;
+  for (int round = 0; round < krem; ++round) {
+    double best = -INFINITY;
+    int bj = 0x7fffffff;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      if (((eligible & ~sel) >> m) & 1u) {
+        const int j = lane + 32 * m;
+        if (better(sc[m], j, best, bj)) {
+          best = sc[m];
+          bj = j;
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+      if (better(ob, oj, best, bj)) {
+        best = ob;
+        bj = oj;
+      }
+    }
+    if (bj == 0x7fffffff) break;  // no candidate left
+    if ((bj & 31) == lane) sel |= 1u << (bj >> 5);
+  }
+  sel |= forced;
+  int base = 0;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const uint32_t bal = __ballot_sync(0xffffffffu, (sel >> m) & 1u);
+    if ((sel >> m) & 1u) {
+      const int pos = base + __popc(bal & ((1u << lane) - 1u));
+      a.padded[rbase + pos] = lane + 32 * m;
+    }
+    base += __popc(bal);
+    const int j = lane + 32 * m;
+    if (j < a.nbk) {
+      if (a.mask_out) a.mask_out[rbase + j] = (sel >> m) & 1u;
+      if (a.score_out) a.score_out[rbase + j] = sc[m];
+    }
+  }
+  if (lane == 0) a.counts[static_cast<int64_t>(g) * a.nbq + row] = base;
 }
 
-// grid (B*H), 256 threads: per-head exclusive scan of the row counts, then a
-// copy of each row's columns into its CSR slot.
+// grid (B*H, ceil(nbq / 8)), 256 threads.  Every CTA redoes the (small)
+// exclusive scan of its head's row counts, then one warp per row copies that
+// row's columns into its CSR slot.  CTA y == 0 also writes the head's row_ptr.
 __global__ void __launch_bounds__(256) csr_compact_kernel(int nbq, int nbk,
                                                           const int32_t* __restrict__ counts,
                                                           const int32_t* __restrict__ padded,
@@ -214,7 +230,6 @@ __global__ void __launch_bounds__(256) csr_compact_kernel(int nbq, int nbk,
   const int g = blockIdx.x;
   const int64_t seg = static_cast<int64_t>(g) * nbq * nbk;
   const int32_t* cnt = counts + static_cast<int64_t>(g) * nbq;
-  // nbq <= 1024: each thread scans up to 4 consecutive rows.
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int local[4], tot = 0;
 #pragma unroll
@@ -240,11 +255,14 @@ __global__ void __launch_bounds__(256) csr_compact_kernel(int nbq, int nbk,
     if (r < nbq) pref[r] = run;
     run += local[e];
   }
-  if (tid == 255) pref[nbq] = run;  // last thread holds the grand total
+  if (tid == 255) pref[nbq] = run;  // the last thread holds the grand total
   __syncthreads();
-  int32_t* rp = row_ptr + static_cast<int64_t>(g) * (nbq + 1);
-  for (int r = tid; r <= nbq; r += 256) rp[r] = static_cast<int32_t>(seg + pref[r]);
-  for (int r = warp; r < nbq; r += 8) {
+  if (blockIdx.y == 0) {
+    int32_t* rp = row_ptr + static_cast<int64_t>(g) * (nbq + 1);
+    for (int r = tid; r <= nbq; r += 256) rp[r] = static_cast<int32_t>(seg + pref[r]);
+  }
+  const int r = blockIdx.y * 8 + warp;
+  if (r < nbq) {
     const int n = pref[r + 1] - pref[r];
     const int32_t* src = padded + seg + static_cast<int64_t>(r) * nbk;
     int32_t* dst = col_idx + seg + pref[r];
@@ -313,15 +331,24 @@ SelectLayout select_layout(int64_t BH, int nbq, int nbk, int D) {
 }
 
 template <typename T>
-void launch_pool(const saf_tensor4* t, int block, int nb, double* out, cudaStream_t st) {
+int32_t launch_pool_t(const saf_tensor4* q, const saf_tensor4* k, int bm, int bn, int nbq, int nbk,
+                      double* qbar, double* kbar, cudaStream_t st) {
   constexpr int VEC = 16 / sizeof(T);
-  const int vpr = static_cast<int>(t->D) / VEC;
+  const int D = static_cast<int>(q->D);
+  const int vpr = D / VEC;
   const int groups = kPoolThreads / vpr;
-  const size_t smem = static_cast<size_t>(groups) * t->D * sizeof(double);
-  dim3 grid(nb, static_cast<unsigned>(t->B * t->H));
-  pool_mean_kernel<T><<<grid, kPoolThreads, smem, st>>>(
-      static_cast<const T*>(t->data), static_cast<int>(t->H), static_cast<int>(t->S),
-      static_cast<int>(t->D), t->stride_b, t->stride_h, t->stride_s, block, out);
+  const size_t smem = static_cast<size_t>(groups) * D * sizeof(double);
+  PoolOperand qo{q->data, static_cast<int>(q->S), q->stride_b, q->stride_h, q->stride_s, bm, nbq, qbar};
+  PoolOperand ko{k->data, static_cast<int>(k->S), k->stride_b, k->stride_h, k->stride_s, bn, nbk, kbar};
+  dim3 grid(nbq > nbk ? nbq : nbk, static_cast<unsigned>(q->B * q->H), 2);
+  // rows per thread per pass: the whole block in one pass when it fits in 8
+  const int bmax = bm > bn ? bm : bn;
+  if ((bmax + groups - 1) / groups <= 4) {
+    pool_mean_kernel<T, 4><<<grid, kPoolThreads, smem, st>>>(qo, ko, static_cast<int>(q->H), D);
+  } else {
+    pool_mean_kernel<T, 8><<<grid, kPoolThreads, smem, st>>>(qo, ko, static_cast<int>(q->H), D);
+  }
+  return SAF_OK;
 }
 
 int32_t check_pool_operand(const saf_tensor4* t) {
@@ -336,13 +363,23 @@ int32_t check_pool_operand(const saf_tensor4* t) {
   return SAF_OK;
 }
 
-int32_t pool_dispatch(const saf_tensor4* t, int block, int nb, double* out, cudaStream_t st) {
-  switch (t->dtype) {
-    case SAF_BF16: launch_pool<__nv_bfloat16>(t, block, nb, out, st); break;
-    case SAF_F16: launch_pool<__half>(t, block, nb, out, st); break;
-    case SAF_F32: launch_pool<float>(t, block, nb, out, st); break;
+int32_t pool_dispatch(const saf_tensor4* q, const saf_tensor4* k, int bm, int bn, int nbq, int nbk,
+                      double* qbar, double* kbar, cudaStream_t st) {
+  switch (q->dtype) {
+    case SAF_BF16: return launch_pool_t<__nv_bfloat16>(q, k, bm, bn, nbq, nbk, qbar, kbar, st);
+    case SAF_F16: return launch_pool_t<__half>(q, k, bm, bn, nbq, nbk, qbar, kbar, st);
+    case SAF_F32: return launch_pool_t<float>(q, k, bm, bn, nbq, nbk, qbar, kbar, st);
     default: return SAF_ERR_DTYPE;
   }
+}
+
+template <int M>
+int32_t launch_score(const SelectArgs& a, int64_t BH, cudaStream_t st) {
+  const size_t smem = (static_cast<size_t>(a.nbk) + 8) * (kDChunk + 1) * sizeof(double);
+  SAF_CUDA_TRY(cudaFuncSetAttribute(score_topk_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+  dim3 grid(static_cast<unsigned>(BH), (a.nbq + 7) / 8);
+  score_topk_kernel<M><<<grid, 256, smem, st>>>(a);
   return SAF_OK;
 }
 
@@ -368,7 +405,6 @@ extern "C" int32_t saf_pool_topk(const saf_tensor4* q, const saf_tensor4* k,
   int32_t rc;
   if ((rc = check_pool_operand(q)) != SAF_OK) return rc;
   if ((rc = check_pool_operand(k)) != SAF_OK) return rc;
-  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
   if (q->dtype != k->dtype) return SAF_ERR_DTYPE;
   if (q->B != k->B || q->H != k->H || q->D != k->D) return SAF_ERR_SHAPE;
   if (cfg->block_m <= 0 || cfg->block_n <= 0 || cfg->topk < 0 || cfg->text_blocks_q < 0 ||
@@ -385,12 +421,13 @@ extern "C" int32_t saf_pool_topk(const saf_tensor4* q, const saf_tensor4* k,
   const SelectLayout lay = select_layout(BH, nbq, nbk, D);
   if (workspace == nullptr || workspace_bytes < lay.total) return SAF_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return SAF_ERR_WORKSPACE;
+  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   double* qbar = reinterpret_cast<double*>(ws + lay.off_qbar);
   double* kbar = reinterpret_cast<double*>(ws + lay.off_kbar);
-  if ((rc = pool_dispatch(q, cfg->block_m, nbq, qbar, st)) != SAF_OK) return rc;
-  if ((rc = pool_dispatch(k, cfg->block_n, nbk, kbar, st)) != SAF_OK) return rc;
+  if ((rc = pool_dispatch(q, k, cfg->block_m, cfg->block_n, nbq, nbk, qbar, kbar, st)) != SAF_OK)
+    return rc;
   SAF_CUDA_TRY(cudaGetLastError());
 
   SelectArgs a{};
@@ -408,14 +445,13 @@ extern "C" int32_t saf_pool_topk(const saf_tensor4* q, const saf_tensor4* k,
   a.counts = reinterpret_cast<int32_t*>(ws + lay.off_counts);
   a.mask_out = mask_out;
   a.score_out = score_out;
-  const size_t smem = (static_cast<size_t>(nbk) + kRowsPerCta) * (kDChunk + 1) * sizeof(double);
-  SAF_CUDA_TRY(cudaFuncSetAttribute(score_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem)));
-  dim3 grid(static_cast<unsigned>(BH), (nbq + kRowsPerCta - 1) / kRowsPerCta);
-  score_topk_kernel<<<grid, 256, smem, st>>>(a);
+  if (nbk <= 160) rc = launch_score<5>(a, BH, st);
+  else if (nbk <= 288) rc = launch_score<9>(a, BH, st);
+  else rc = launch_score<16>(a, BH, st);
+  if (rc != SAF_OK) return rc;
   SAF_CUDA_TRY(cudaGetLastError());
-  csr_compact_kernel<<<static_cast<unsigned>(BH), 256, 0, st>>>(nbq, nbk, a.counts, a.padded,
-                                                                row_ptr, col_idx);
+  csr_compact_kernel<<<dim3(static_cast<unsigned>(BH), (nbq + 7) / 8), 256, 0, st>>>(
+      nbq, nbk, a.counts, a.padded, row_ptr, col_idx);
   SAF_CUDA_TRY(cudaGetLastError());
   return SAF_OK;
 }

@@ -1,0 +1,140 @@
+"""Generates the golden fixtures that pin the CPU oracle to the reference.
+
+Run where the reference source tree is available (it is not on the GPU box):
+
+    python tests/golden/make_golden.py [/path/to/SparseAttnFunctions]
+
+It imports the reference's own Python modules from that tree -- with stub
+modules for the imports this path does not use (sageattention, torch_kmeans,
+matplotlib, torchmetrics and the external ``global_vars``) -- runs them on
+the CPU on seeded inputs and writes ``tests/golden/*.npz``.  Inputs are not
+stored: they are regenerated from ``numpy.random.RandomState(seed)`` (whose
+streams numpy keeps stable), so the fixtures hold only seeds, parameters and
+the reference's outputs.
+
+Fixtures
+  topk_masks.npz    get_sparse_attn_mask_from_topk (block_sparse_attn_kernel.py:31-39)
+  energy_masks.npz  transfer_attn_to_mask(mode="energy") (SparseGen_Plus.py:12-84)
+  tome_*.npz        bipartite_soft_matching_video + merge / unmerge
+                    (utils/merge_unmerge.py:34-154), fp64 metric
+"""
+from __future__ import annotations
+
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def import_reference(root: str):
+    for name in ["sageattention", "torch_kmeans", "matplotlib", "matplotlib.pyplot", "torchmetrics",
+                 "torchmetrics.functional", "global_vars"]:
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.modules["sageattention"].sageattn = None
+    sys.modules["torch_kmeans"].KMeans = None
+    sys.modules["matplotlib"].use = lambda *a, **k: None
+    sys.modules["matplotlib"].pyplot = sys.modules["matplotlib.pyplot"]
+    sys.modules["torchmetrics.functional"].mean_squared_error = None
+    sys.modules["global_vars"].count = 0
+    sys.path.insert(0, root)
+    from special_attentions import SparseGen_Plus
+    from special_attentions.utils import block_sparse_attn_kernel, merge_unmerge
+
+    return block_sparse_attn_kernel, SparseGen_Plus, merge_unmerge
+
+
+def closure_vars(fn):
+    return {name: cell.cell_contents for name, cell in zip(fn.__code__.co_freevars, fn.__closure__)}
+
+
+TOPK_CASES = [  # (seed, B, H, n, topk)
+    (101, 1, 2, 16, 4), (102, 2, 3, 33, 5), (103, 1, 1, 139, 14), (104, 1, 2, 64, 1)]
+ENERGY_CASES = [  # (seed, B, H, n, thr, min_ratio, max_ratio)
+    (201, 1, 2, 20, 0.9, 0.1, 0.8), (202, 2, 2, 45, 0.95, 0.1, 0.7), (203, 1, 3, 139, 0.98, 0.12, 1.0)]
+TOME_CASES = [  # (name, metric seed, C, r, generator seed or None)
+    ("tome_norand_r4000", 11, 8, 4000, None), ("tome_gen_r9000", 12, 8, 9000, 5)]
+GEOM = dict(w=45, h=30, t=13, sx=3, sy=3, st=4)
+TEXT = 226
+PROJ_C = 240  # channel count that lets the reference's unmerge reshape to (2, 30, -1, 64)
+
+
+def topk_input(seed, B, H, n):
+    return np.random.RandomState(seed).randn(B, H, n, n)
+
+
+def energy_input(seed, B, H, n):
+    return np.random.RandomState(seed).rand(B, H, n, n) ** 3
+
+
+def tome_metric(seed, C):
+    return np.random.RandomState(seed).randn(1, GEOM["w"] * GEOM["h"] * GEOM["t"], C)
+
+
+def tome_x(seed, n_rows):
+    return np.random.RandomState(seed + 1000).randn(1, n_rows, PROJ_C)
+
+
+def projection(seed):
+    return np.random.RandomState(seed + 2000).randn(PROJ_C)
+
+
+def main(root: str):
+    import torch
+
+    bsk, sgp, mu = import_reference(root)
+
+    masks = {}
+    for seed, B, H, n, k in TOPK_CASES:
+        x = torch.from_numpy(topk_input(seed, B, H, n))
+        masks[f"case_{seed}"] = bsk.get_sparse_attn_mask_from_topk(x, k).numpy()
+    np.savez_compressed(HERE / "topk_masks.npz", cases=np.array(TOPK_CASES), **masks)
+
+    masks = {}
+    for seed, B, H, n, thr, mn, mx in ENERGY_CASES:
+        a = torch.from_numpy(energy_input(seed, B, H, n))
+        masks[f"case_{seed}"] = sgp.transfer_attn_to_mask(
+            a, mode="energy", max_retain_ratio=mx, min_retain_ratio=mn, energy_threshold=thr).numpy()
+    np.savez_compressed(HERE / "energy_masks.npz", cases=np.array(ENERGY_CASES), **masks)
+
+    for name, seed, C, r, gseed in TOME_CASES:
+        metric = torch.from_numpy(tome_metric(seed, C))
+        gen = None if gseed is None else torch.Generator().manual_seed(gseed)
+        merge, unmerge = mu.bipartite_soft_matching_video(metric, **GEOM, r=r, no_rand=gseed is None,
+                                                          generator=gen)
+        cv = closure_vars(merge)
+        uv = closure_vars(unmerge)
+        sv = closure_vars(cv["split"])
+        a_idx = sv["a_idx"].reshape(-1).numpy()  # video-token indices (reference order)
+        b_idx = sv["b_idx"].reshape(-1).numpy()
+        out = dict(a_idx=a_idx.astype(np.int32), b_idx=b_idx.astype(np.int32),
+                   unm_idx=cv["unm_idx"].reshape(-1).numpy().astype(np.int32),
+                   src_idx=cv["src_idx"].reshape(-1).numpy().astype(np.int32),
+                   dst_idx=cv["dst_idx"].reshape(-1).numpy().astype(np.int32),
+                   counter=mu.counter.reshape(-1).numpy().astype(np.int32),
+                   params=np.array([seed, C, r, -1 if gseed is None else gseed]))
+        if gseed is not None:
+            g = torch.Generator().manual_seed(gseed)
+            tst, hsy, wsx = (GEOM["t"] - 1) // GEOM["st"], GEOM["h"] // GEOM["sy"], GEOM["w"] // GEOM["sx"]
+            out["rand_idx"] = torch.randint(GEOM["sy"] * GEOM["sx"] * GEOM["st"], size=(tst, hsy, wsx, 1),
+                                            generator=g).reshape(-1).numpy().astype(np.int32)
+        # merge of a 3-D tensor and unmerge of [text | merged]: stored as two
+        # projections per row (row sums and a fixed random projection).
+        n = metric.shape[1]
+        proj = torch.from_numpy(projection(seed))
+        x = torch.from_numpy(tome_x(seed, n))
+        merged = merge(x)
+        out["merge_rowsum"] = merged.sum(-1).reshape(-1).numpy()
+        out["merge_proj"] = (merged @ proj).reshape(-1).numpy()
+        y = torch.from_numpy(tome_x(seed + 1, TEXT + merged.shape[1]))
+        un = unmerge(y).reshape(1, -1, PROJ_C)
+        out["unmerge_rowsum"] = un.sum(-1).reshape(-1).numpy()
+        out["unmerge_proj"] = (un @ proj).reshape(-1).numpy()
+        np.savez_compressed(HERE / f"{name}.npz", **out)
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

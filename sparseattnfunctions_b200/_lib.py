@@ -10,10 +10,13 @@ as ``ValueError``; CUDA failures as ``RuntimeError``).
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libsaf.so"
+# The in-tree build; SAF_LIBRARY may point at another build of the same ABI
+# (used to compare kernel variants side by side).
+LIB_PATH = Path(os.environ.get("SAF_LIBRARY") or Path(__file__).resolve().parent / "libsaf.so")
 
 SAF_OK = 0
 SAF_ERR_SHAPE = 1

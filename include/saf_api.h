@@ -103,6 +103,22 @@ int32_t saf_pool_topk(const saf_tensor4* q, const saf_tensor4* k, const saf_sele
                       int32_t* row_ptr, int32_t* col_idx, uint8_t* mask_out, double* score_out,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Block selection without a workspace argument.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when
+ * they call in (memory planned once and frozen, plugin slots that receive
+ * only their inputs and outputs, loops that must not synchronise on
+ * cudaMalloc).  Same results as saf_pool_topk; the scratch comes from a
+ * static SAF_STATIC_SCRATCH_BYTES device array that every GPU loading this
+ * library holds until the process exits.  Returns SAF_ERR_WORKSPACE when the
+ * problem needs more scratch than that (saf_pool_topk_workspace_bytes tells
+ * how much).  Allocates nothing.  The first call on each device looks up the
+ * array's device address (make that first call before any stream capture).
+ * All calls share the array: calls that overlap on the GPU race. */
+#define SAF_STATIC_SCRATCH_BYTES (16u << 20) /* 16 MiB */
+int32_t saf_pool_topk_noalloc(const saf_tensor4* q, const saf_tensor4* k,
+                              const saf_select_cfg* cfg, int32_t* row_ptr, int32_t* col_idx,
+                              uint8_t* mask_out, double* score_out, void* stream);
+
 /* Dense boolean block mask [BH, nbq, nbk] (uint8, element strides
  * stride_bh / stride_row, column stride 1) -> segmented CSR as above.
  * Replaces the dense-mask walk of _fwd_kernel

@@ -21,6 +21,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "saf_common.cuh"
 
 namespace saf {
@@ -471,4 +473,62 @@ extern "C" int32_t saf_mask_to_csr(const uint8_t* mask, int64_t BH, int32_t nbq,
       mask, nbq, nbk, stride_bh, stride_row, row_ptr, col_idx);
   SAF_CUDA_TRY(cudaGetLastError());
   return SAF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Scratch-free block selection.
+//
+// saf_pool_topk needs a caller-provided workspace.  Some callers cannot
+// allocate device memory at the moment they call in: a host process whose
+// memory is planned once at start-up and then frozen, a plugin slot that is
+// handed only its input and output buffers, or a latency-critical loop that
+// must not pay for (or implicitly synchronise on) cudaMalloc.  For them,
+// saf_pool_topk_noalloc runs the same kernels with the workspace taken from
+// the static array below, which the CUDA module creates on every device that
+// loads this library and keeps until the process exits.
+//
+// The array's name is meaningful only to device code.  Host code must use the
+// device address that cudaGetSymbolAddress returns for the current device;
+// that lookup happens on the first call for each device (with that device
+// current) and is cached.  Nothing in the array has to start at zero: every
+// byte the kernels read is written earlier in the same call, so stale data
+// from a previous call is harmless.  All calls share the one array, so calls
+// whose work overlaps on the GPU (other streams, other host threads) race.
+static __device__ __align__(256) unsigned char saf_select_static_scratch[SAF_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_ptr[64] = {nullptr};
+
+int32_t static_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SAF_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (g_static_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, saf_select_static_scratch) != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      return SAF_ERR_CUDA;
+    }
+    g_static_scratch_ptr[dev] = ptr;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return SAF_OK;
+}
+}  // namespace
+
+extern "C" int32_t saf_pool_topk_noalloc(const saf_tensor4* q, const saf_tensor4* k,
+                                         const saf_select_cfg* cfg, int32_t* row_ptr,
+                                         int32_t* col_idx, uint8_t* mask_out, double* score_out,
+                                         void* stream) {
+  if (q == nullptr || k == nullptr || cfg == nullptr || q->data == nullptr) return SAF_ERR_ARG;
+  const size_t need = saf_pool_topk_workspace_bytes(q, k, cfg);
+  if (need == 0) return SAF_ERR_ARG;
+  if (need > SAF_STATIC_SCRATCH_BYTES) return SAF_ERR_WORKSPACE;  // problem too large for it
+  int32_t rc = bind_device_of(q->data);
+  if (rc != SAF_OK) return rc;
+  void* scratch = nullptr;
+  if ((rc = static_scratch_address(&scratch)) != SAF_OK) return rc;
+  return saf_pool_topk(q, k, cfg, row_ptr, col_idx, mask_out, score_out, scratch,
+                       SAF_STATIC_SCRATCH_BYTES, stream);
 }

@@ -137,6 +137,10 @@ int32_t saf_mask_to_csr(const uint8_t* mask, int64_t BH, int32_t nbq, int32_t nb
  * broadcasts one row).  Rows with no live block give NaN (0/0), as the
  * reference kernel does.
  * col_capacity bounds every col_idx read (entries past it are ignored).
+ * lead_rows: query blocks [0, lead_rows) of every head are scheduled before
+ * all others -- pass the number of dense (text) rows, whose block lists are
+ * the longest, so they do not start last and stretch the tail; 0 keeps
+ * head-major order.  Results do not depend on it.
  * Replaces: _forward / _fwd_kernel / _fwd_kernel_inner /
  * block_sparse_triton_fn (utils/block_sparse_attn_kernel.py:52-293) and the
  * bias path of MergeAttention.forward (MergeAttention.py:33-49). */
@@ -144,7 +148,7 @@ int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor
                     const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                     int64_t col_capacity, int32_t block_m, int32_t block_n,
                     const float* kv_bias, int64_t kv_bias_stride_bh, float sm_scale,
-                    void* stream);
+                    int32_t lead_rows, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -15,7 +15,7 @@ namespace saf {
 int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
-                      int64_t bias_stride, float sm_scale, cudaStream_t stream);
+                      int64_t bias_stride, float sm_scale, int lead_tiles, cudaStream_t stream);
 
 namespace {
 
@@ -252,7 +252,7 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
                                const saf_tensor4* o, const int32_t* row_ptr,
                                const int32_t* col_idx, int64_t col_capacity, int32_t block_m,
                                int32_t block_n, const float* kv_bias, int64_t kv_bias_stride_bh,
-                               float sm_scale, void* stream) {
+                               float sm_scale, int32_t lead_rows, void* stream) {
   int32_t rc = check_tensor4(q);
   if (rc != SAF_OK) return rc;
   if ((rc = check_operand(k, q)) != SAF_OK) return rc;
@@ -262,6 +262,7 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
   if (row_ptr == nullptr || col_idx == nullptr || col_capacity < 0) return SAF_ERR_ARG;
   if (block_m <= 0 || block_n <= 0) return SAF_ERR_ARG;
   if (kv_bias_stride_bh < 0) return SAF_ERR_STRIDE;
+  if (lead_rows < 0) return SAF_ERR_ARG;
   if (q->S > 0x7fffffff || k->S > 0x7fffffff || q->B * q->H > 65535) return SAF_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (q->dtype == SAF_F32) {
@@ -280,6 +281,9 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
       return SAF_ERR_STRIDE;
   }
   if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
+  // Leading mask rows -> leading 128-row query tiles scheduled first.
+  const int64_t lead_tiles = (static_cast<int64_t>(lead_rows) * block_m + 127) / 128;
   return bsa_fwd_sm100(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
-                       kv_bias_stride_bh, sm_scale, st);
+                       kv_bias_stride_bh, sm_scale,
+                       static_cast<int>(lead_tiles < 65535 ? lead_tiles : 65535), st);
 }

@@ -67,6 +67,7 @@ struct BsaParams {
   int64_t o_sb, o_sh, o_ss;  // element strides
   unsigned int* status;
   uint64_t budget_ns;
+  int lead_tiles;  // query tiles per head scheduled first
 };
 
 // Iterates the live kv tiles of one 128-row query tile.  With 64-row mask
@@ -171,8 +172,23 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
-  const int g = blockIdx.y;
+  // Launch order: the first `lead_tiles` query tiles of every head (dense
+  // text rows, the longest block lists) go first, tile-major; the rest run
+  // head-major so that CTAs resident together share a head's K/V in L2.
+  int tile, g;
+  {
+    const int n_tiles = gridDim.x, BH = gridDim.y;
+    const int lin = blockIdx.x + blockIdx.y * n_tiles;
+    const int lead = p.lead_tiles < n_tiles ? p.lead_tiles : n_tiles;
+    if (lin < lead * BH) {
+      tile = lin / BH;
+      g = lin % BH;
+    } else {
+      const int rest = n_tiles - lead, l2 = lin - lead * BH;
+      g = l2 / rest;
+      tile = lead + l2 % rest;
+    }
+  }
   const int b = g / p.H, h = g % p.H;
   const int q0 = tile * kBM;
 
@@ -427,10 +443,66 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int e = 0; e < HC; ++e)
           if (!(live && e < valid)) t[e] = -INFINITY;
       }
-      // Local max of this half row: four running 3-input-max accumulators
-      // (no temporary array next to the live scores).
-      float mx;
-      {
+      // Under lazy rescaling the running max rarely moves, so P is computed
+      // speculatively with the current running max while the block max is
+      // accumulated alongside (ALU work next to the MUFU work).  The pair then
+      // exchanges maxima; only if a row's max jumped past the threshold does
+      // the warp recompute P (the scores are still in registers) and rescale
+      // O.  A warp with a row that has not seen a live score yet takes the
+      // max-first order.
+      const bool spec = __all_sync(0xffffffffu, m_run != -INFINITY);
+      bool pv_done = (j == 0);
+      // PV of the previous block must be done before P is overwritten and
+      // before O is rescaled.
+      auto wait_pv = [&]() -> bool {
+        if (pv_done) return true;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status,
+                                                p.budget_ns)))
+          return false;
+        tc_fence_after();
+        pv_done = true;
+        return true;
+      };
+      f2 rs = mk2(0.f, 0.f);
+      float mx = -INFINITY;
+      // P = exp2(logit - m) in the input type, row sum in fp32 pairs, 32
+      // scores at a time (the empty asm after each store keeps the next part's
+      // exp2 from being scheduled early, bounding live registers).
+      auto exp_pass = [&](float neg_m, bool with_max) -> bool {
+        const f2 negm2 = mk2(neg_m, neg_m);
+        rs = mk2(0.f, 0.f);
+        float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < HC / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (with_max)
+              acc[e & 3] = fmax3(acc[e & 3], t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
+            f2 x = mk2(t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
+            x = kBias ? add2(x, negm2) : fma2(x, sl2x2, negm2);
+            const float e0 = ex2_approx(lo2(x)), e1 = ex2_approx(hi2(x));
+            rs = add2(rs, mk2(e0, e1));
+            pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
+          }
+          if (c == 0 && !wait_pv()) return false;
+          tmem_st16(tP + c * 16, pk);
+          if (c + 1 < HC / 32) {
+            asm volatile("" : "+l"(rs.v));
+#pragma unroll
+            for (int e = 0; e < 32; ++e) asm volatile("" : "+f"(t[(c + 1) * 32 + e]));
+          }
+        }
+        if (with_max) mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
+        return true;
+      };
+
+      if (spec) {
+        if (!exp_pass(-m_run, true)) {
+          ok = false;
+          break;
+        }
+      } else {
         float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int i = 0; i < HC / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
@@ -451,48 +523,24 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float m_new = upd ? m_cand : m_run;
       const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
       const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
-
-      if (j > 0) {
-        // PV of the previous block must be done before P is overwritten and
-        // before O is rescaled.
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status,
-                                                p.budget_ns))) {
+      const bool any_upd = __any_sync(0xffffffffu, upd);
+      if (!spec || any_upd) {
+        if (!exp_pass(neg_m, false)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, upd)) {
-          uint32_t orr[32];
-          tmem_ld32(tO, orr);
-          tmem_wait_ld(orr);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-          tmem_st32(tO, orr);
-        }
       }
-
-      // P = exp2(logit - m) in the input type; row sum in fp32 pairs.  Done
-      // 32 scores at a time; the empty asm after each store keeps the next
-      // part's exp2 from being scheduled early (bounds live registers).
-      const f2 negm2 = mk2(neg_m, neg_m);
-      f2 rs = mk2(0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < HC / 32; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          f2 x = mk2(t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
-          x = kBias ? add2(x, negm2) : fma2(x, sl2x2, negm2);
-          const float e0 = ex2_approx(lo2(x)), e1 = ex2_approx(hi2(x));
-          rs = add2(rs, mk2(e0, e1));
-          pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
+      if (j > 0 && any_upd) {
+        if (!wait_pv()) {
+          ok = false;
+          break;
         }
-        tmem_st16(tP + c * 16, pk);
-        if (c + 1 < HC / 32) {
-          asm volatile("" : "+l"(rs.v));
+        uint32_t orr[32];
+        tmem_ld32(tO, orr);
+        tmem_wait_ld(orr);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) asm volatile("" : "+f"(t[(c + 1) * 32 + e]));
-        }
+        for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+        tmem_st32(tO, orr);
       }
       l_run = l_run * alpha + (lo2(rs) + hi2(rs));
       m_run = m_new;
@@ -590,7 +638,7 @@ int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
 int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
-                      int64_t bias_stride, float sm_scale, cudaStream_t stream) {
+                      int64_t bias_stride, float sm_scale, int lead_tiles, cudaStream_t stream) {
   if (q->D != kD) return SAF_ERR_UNSUPPORTED;
   if (!current_device_is_sm100()) return SAF_ERR_UNSUPPORTED;
   CUtensorMap mq, mk, mv;
@@ -618,6 +666,7 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   p.o_ss = o->stride_s;
   p.status = device_status_ptr();
   p.budget_ns = wait_budget_ns();
+  p.lead_tiles = lead_tiles;
   if (p.status == nullptr) return SAF_ERR_CUDA;
   const int n_tiles = static_cast<int>((q->S + kBM - 1) / kBM);
   const bool bf16 = q->dtype == SAF_BF16;

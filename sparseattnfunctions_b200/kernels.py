@@ -77,6 +77,7 @@ class BlockCSR:
     block_n: int
     mask: Optional[torch.Tensor] = None    # uint8 [B, H, nbq, nbk] when requested
     scores: Optional[torch.Tensor] = None  # fp64 [B, H, nbq, nbk] when requested
+    dense_rows: int = 0  # leading row blocks that are dense (scheduled first by bsa_fwd)
 
     def nnz_per_head(self) -> torch.Tensor:
         """Live blocks per head (device tensor, no sync)."""
@@ -142,11 +143,13 @@ def pool_topk(q: torch.Tensor, k: torch.Tensor, *, block_m: int, block_n: int, t
                                scores.data_ptr() if scores is not None else None,
                                ws.data_ptr(), ws.numel(), _stream_ptr(dev))
     _lib.check("saf_pool_topk", rc)
-    return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n, mask, scores)
+    return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n, mask, scores,
+                    dense_rows=min(text_blocks_q, nbq))
 
 
-def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int) -> BlockCSR:
-    """Dense boolean block mask ``[B, H, nbq, nbk]`` -> ``BlockCSR``."""
+def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int, dense_rows: int = 0) -> BlockCSR:
+    """Dense boolean block mask ``[B, H, nbq, nbk]`` -> ``BlockCSR``.  ``dense_rows``
+    tells ``bsa_fwd`` how many leading row blocks have the longest lists."""
     dev = _require_cuda(block_mask)
     if block_mask.dim() != 4:
         raise ValueError("block mask must be [B, H, nbq, nbk]")
@@ -164,7 +167,7 @@ def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int) -> BlockCS
         rc = _lib.load().saf_mask_to_csr(m.data_ptr(), B * H, nbq, nbk, m.stride(1), m.stride(2),
                                          row_ptr.data_ptr(), col_idx.data_ptr(), _stream_ptr(dev))
     _lib.check("saf_mask_to_csr", rc)
-    return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n)
+    return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n, dense_rows=dense_rows)
 
 
 def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm_scale: float,
@@ -202,6 +205,7 @@ def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm
         rc = _lib.load().saf_bsa_fwd(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
                                      ctypes.byref(to), csr.row_ptr.data_ptr(), csr.col_idx.data_ptr(),
                                      csr.col_idx.numel(), csr.block_m, csr.block_n, bias_ptr,
-                                     bias_stride, float(sm_scale), _stream_ptr(dev))
+                                     bias_stride, float(sm_scale), int(csr.dense_rows),
+                                     _stream_ptr(dev))
     _lib.check("saf_bsa_fwd", rc)
     return out

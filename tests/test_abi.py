@@ -69,7 +69,7 @@ def test_bsa_rejects_bad_arguments_on_host(lib):
     q, k, v, o = _t4(data=good), _t4(data=good), _t4(data=good), _t4(data=good)
     args = lambda q_, k_, v_, o_, rp=good, ci=good: lib.saf_bsa_fwd(
         ctypes.byref(q_), ctypes.byref(k_), ctypes.byref(v_), ctypes.byref(o_), rp, ci, 16, 128, 128,
-        None, 0, 0.125, None)
+        None, 0, 0.125, 0, None)
     assert args(_t4(data=0), k, v, o) == _lib.SAF_ERR_ARG            # null data
     assert args(q, k, v, o, rp=None) == _lib.SAF_ERR_ARG             # null CSR
     assert args(_t4(data=good, dtype=9), k, v, o) == _lib.SAF_ERR_DTYPE
@@ -79,6 +79,8 @@ def test_bsa_rejects_bad_arguments_on_host(lib):
     bad = _t4(data=good)
     bad.stride_s = 10  # < D
     assert args(bad, k, v, o) == _lib.SAF_ERR_STRIDE
+    assert lib.saf_bsa_fwd(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v), ctypes.byref(o), good,
+                           good, 16, 128, 128, None, 0, 0.125, -1, None) == _lib.SAF_ERR_ARG
 
 
 def test_pool_topk_rejects_bad_arguments_on_host(lib):

@@ -171,3 +171,20 @@ def test_rejects_cpu_tensors():
     q = torch.zeros(1, 1, 64, 64, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         kernels.bsa_fwd(q, q, q, None, 0.125)
+
+
+@pytest.mark.parametrize("bm", [128, 64])
+def test_lead_rows_schedule_does_not_change_results(cuda_device, bm):
+    """The dense-row scheduling hint only reorders CTAs: outputs are bitwise
+    identical for any value."""
+    B, H, S, D = 2, 3, 1500, 64
+    q, k, v = (t.to(cuda_device) for t in _inputs(B, H, S, S, D, torch.bfloat16, seed=41))
+    nb = math.ceil(S / bm)
+    mask = _random_mask(B, H, nb, nb, 0.3, seed=41).to(cuda_device)
+    mask[:, :, :3, :] = True
+    outs = []
+    for lead in (0, 3, 100):
+        csr = kernels.mask_to_csr(mask, bm, bm, dense_rows=lead)
+        outs.append(kernels.bsa_fwd(q, k, v, csr, 0.125))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])

@@ -140,6 +140,42 @@ struct TileIter {
   }
 };
 
+// exp2 on the FMA pipe (for part of the elements, to offload the MUFU):
+// 2^x = 2^n * 2^f with n = rint(x) (from adding 1.5 * 2^23) and
+// f = x - n in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients
+// minimise the maximum relative error on [-1/2, 1/2] (Remez exchange; max
+// relative error 7.5e-5 in fp32 -- below bf16 and f16 rounding of P); 2^n
+// inserted into the exponent field with one integer multiply-add.  x is
+// clamped to -126 so masked (-inf) and vanishing scores give a tiny
+// positive number instead of a wrapped exponent.
+constexpr float kExp2C0 = 0.9999280571937561f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.2426111251115799f;
+constexpr float kExp2C3 = 0.0551716685295105f;
+constexpr float kRoundShift = 12582912.0f;  // 1.5 * 2^23
+
+__device__ __forceinline__ f2 exp2_poly2(f2 x) {
+  x = mk2(fmaxf(lo2(x), -126.f), fmaxf(hi2(x), -126.f));
+  const f2 t = add2(x, mk2(kRoundShift, kRoundShift));       // n in the low mantissa bits
+  const f2 n = add2(t, mk2(-kRoundShift, -kRoundShift));     // rint(x)
+  const f2 f = fma2(n, mk2(-1.f, -1.f), x);                  // x - n
+  f2 q = fma2(mk2(kExp2C3, kExp2C3), f, mk2(kExp2C2, kExp2C2));
+  q = fma2(q, f, mk2(kExp2C1, kExp2C1));
+  q = fma2(q, f, mk2(kExp2C0, kExp2C0));
+  uint32_t lo, hi;
+  // bits(t) << 23 == n << 23 (the shift constant's low 9 bits are zero)
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(lo) : "r"(__float_as_uint(lo2(t))), "r"(__float_as_uint(lo2(q))));
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(hi) : "r"(__float_as_uint(hi2(t))), "r"(__float_as_uint(hi2(q))));
+  return mk2(__uint_as_float(lo), __uint_as_float(hi));
+}
+
+// Pairs e of every 16-pair chunk whose exp2 runs on the FMA pipe (bit e of
+// the mask); the others use the MUFU.
+#ifndef SAF_EXP2_FMA_MASK
+#define SAF_EXP2_FMA_MASK 0x0000u  // measured slower when the kernel is not MUFU-bound
+#endif
+__host__ __device__ constexpr bool exp2_on_fma(int e) { return (SAF_EXP2_FMA_MASK >> e) & 1u; }
+
 template <int BN>
 struct Layout {
   static constexpr int kQBytes = kBM * kD * 2;  // 16 KB
@@ -468,8 +504,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       // P = exp2(logit - m) in the input type, row sum in fp32 pairs, 32
       // scores at a time (the empty asm after each store keeps the next part's
       // exp2 from being scheduled early, bounding live registers).
-      auto exp_pass = [&](float neg_m, bool with_max) -> bool {
+      // keep: 0 zeroes P of a row with no live score yet (the polynomial maps
+      // -inf to 2^-126, not 0), keeping such rows at l = 0 as the reference.
+      auto exp_pass = [&](float neg_m, bool with_max, float keep) -> bool {
         const f2 negm2 = mk2(neg_m, neg_m);
+        const f2 keep2 = mk2(keep, keep);
         rs = mk2(0.f, 0.f);
         float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -481,7 +520,20 @@ __global__ void __launch_bounds__(kThreads, 2)
               acc[e & 3] = fmax3(acc[e & 3], t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
             f2 x = mk2(t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
             x = kBias ? add2(x, negm2) : fma2(x, sl2x2, negm2);
-            const float e0 = ex2_approx(lo2(x)), e1 = ex2_approx(hi2(x));
+            float e0, e1;
+            if (exp2_on_fma(e)) {
+              const f2 y = exp2_poly2(x);
+              e0 = lo2(y);
+              e1 = hi2(y);
+            } else {
+              e0 = ex2_approx(lo2(x));
+              e1 = ex2_approx(hi2(x));
+            }
+            if (!with_max) {
+              const f2 z = mul2(mk2(e0, e1), keep2);
+              e0 = lo2(z);
+              e1 = hi2(z);
+            }
             rs = add2(rs, mk2(e0, e1));
             pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
           }
@@ -498,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
 
       if (spec) {
-        if (!exp_pass(-m_run, true)) {
+        if (!exp_pass(-m_run, true, 1.f)) {
           ok = false;
           break;
         }
@@ -525,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
       const bool any_upd = __any_sync(0xffffffffu, upd);
       if (!spec || any_upd) {
-        if (!exp_pass(neg_m, false)) {
+        if (!exp_pass(neg_m, false, m_new == -INFINITY ? 0.f : 1.f)) {
           ok = false;
           break;
         }

@@ -339,6 +339,11 @@ __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.v) : "l"(a.v), "l"(b.v), "l"(c.v));
   return d;
 }
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
+  return d;
+}
 __device__ __forceinline__ f2 add2(f2 a, f2 b) {
   f2 d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));

@@ -150,6 +150,66 @@ int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor
                     const float* kv_bias, int64_t kv_bias_stride_bh, float sm_scale,
                     int32_t lead_rows, void* stream);
 
+/* ---- (3) ToMe token merging -----------------------------------------
+ * Output buffers of a bipartite matching.  Positions refer to the src list
+ * a_idx (length Ns) and the dst list b_idx (length Nd) of video tokens.
+ *   unm_idx   [B, Ns-r]  src positions kept, in edge order (node_max desc)
+ *   src_idx   [B, r]     src positions merged, in edge order
+ *   dst_idx   [B, r]     dst position each of them merges into
+ *   counter   [B, Nd]    1 + number of src merged into each dst
+ *   dst_ptr   [B, Nd+1]  CSR over dst_src (offsets within the batch row)
+ *   dst_src   [B, r]     merged src positions grouped by dst, edge order
+ *   token_map [B, N]     (nullable) merged-sequence row of every video token
+ *   log_count [B, Nd]    (nullable) log(counter) in fp32, the proportional-
+ *                        attention bias of the dst columns
+ *   node_max  [B, Ns]    (nullable) exact fp64 best cosine of every src
+ *   node_idx  [B, Ns]    (nullable) its dst position */
+typedef struct saf_tome_plan {
+  int32_t* unm_idx;
+  int32_t* src_idx;
+  int32_t* dst_idx;
+  int32_t* counter;
+  int32_t* dst_ptr;
+  int32_t* dst_src;
+  int32_t* token_map;
+  float* log_count;
+  double* node_max;
+  int32_t* node_idx;
+} saf_tome_plan;
+
+/* Bipartite soft matching of the video tokens of metric [B, N, C]
+ * (bf16/f16, element strides stride_b / stride_n, C contiguous): cosine
+ * similarity of every src (a_idx) with every dst (b_idx) token, best dst per
+ * src, src sorted by it, the first r merged.  Exact contract: fp64 cosine of
+ * the input values, arg-max ties to the lower dst position, sort ties to the
+ * lower src position.  Tensor cores score all pairs, no score matrix is
+ * written to memory.  r larger than Ns is clamped to Ns.
+ * Replaces: bipartite_soft_matching_video (utils/merge_unmerge.py:34-116). */
+size_t saf_tome_match_workspace_bytes(int64_t B, int64_t Ns, int64_t Nd, int64_t C, int32_t r);
+int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, int64_t N, int64_t C,
+                       int64_t stride_b, int64_t stride_n, const int32_t* a_idx, int64_t Ns,
+                       const int32_t* b_idx, int64_t Nd, int32_t r, const saf_tome_plan* plan,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* merge: x [B, text_len + N, C] -> out [B, text_len + (Ns-r) + Nd, C]:
+ * text rows copied, then the kept src tokens (unm_idx order), then every dst
+ * token averaged with the src merged into it (fp32 sum in edge order /
+ * counter; the reference's scatter_reduce "mean" with include_self).
+ * Replaces: merge (utils/merge_unmerge.py:119-135). */
+int32_t saf_tome_merge(const void* x, void* out, int32_t dtype, int64_t B, int64_t C,
+                       int64_t x_stride_b, int64_t x_stride_n, int64_t o_stride_b,
+                       int64_t o_stride_n, int32_t text_len, const int32_t* a_idx, int64_t Ns,
+                       const int32_t* b_idx, int64_t Nd, int32_t r, const saf_tome_plan* plan,
+                       void* stream);
+
+/* unmerge: y [B, text_len + (Ns-r) + Nd, C] -> out [B, text_len + N, C]:
+ * every video token reads its merged row (token_map).
+ * Replaces: unmerge (utils/merge_unmerge.py:137-154). */
+int32_t saf_tome_unmerge(const void* y, void* out, int32_t dtype, int64_t B, int64_t C,
+                         int64_t y_stride_b, int64_t y_stride_n, int64_t o_stride_b,
+                         int64_t o_stride_n, int32_t text_len, int64_t N, const int32_t* token_map,
+                         void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

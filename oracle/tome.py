@@ -17,9 +17,11 @@ closures (special_attentions/utils/merge_unmerge.py:34-154) in numpy:
   first r are merged (``src_idx``, ``dst_idx``), the rest stay
   (``unm_idx``); ``counter`` = 1 + number of src merged into each dst.
   Contract of this build (the reference's bf16 scores are tie-dominated):
-  cos(a, b) = dot(a, b) / (sqrt(|a|^2) * sqrt(|b|^2)) in fp64 on the exact
-  input values (sums of exact products, correctly rounded sqrt / mul / div);
-  arg-max ties -> lower dst position; sort ties -> lower src position.
+  cos(a, b) = dot(a, b) / (sqrt(|a|^2) * sqrt(|b|^2)) in fp64 on the input
+  values, every dot product summed in the kernels' fixed order (``lane_dot``:
+  exact products, per-lane ascending sums, xor butterfly), correctly rounded
+  sqrt / mul / div; arg-max ties -> lower dst position; sort ties -> lower
+  src position.
 * merge (:119-135): ``[unm, scatter_reduce(dst, dst_idx, src, "mean")]``
   with ``include_self`` (so dst_j = (dst_j + sum of its src) / counter_j);
   the 4-D form prepends the text tokens (:120-128).
@@ -66,8 +68,30 @@ def alternate_split(n: int):
     return idx[0::2].copy(), idx[1::2].copy()
 
 
+def lane_dot(x, y) -> np.ndarray:
+    """fp64 dot products over the last axis in the summation order of the
+    CUDA kernels: 32 lanes each add the exact products of columns
+    c = lane, lane + 32, ... in ascending order, then the lane sums are
+    combined by an xor butterfly (offsets 16, 8, 4, 2, 1).  Products of
+    16-bit values are exact in fp64, so this order fixes every rounding."""
+    prod = np.asarray(x, np.float64) * np.asarray(y, np.float64)
+    C = prod.shape[-1]
+    Cp = -(-C // 32) * 32
+    if Cp != C:
+        prod = np.concatenate([prod, np.zeros(prod.shape[:-1] + (Cp - C,))], axis=-1)
+    prod = prod.reshape(prod.shape[:-1] + (Cp // 32, 32))
+    p = np.zeros(prod.shape[:-2] + (32,))
+    for k in range(Cp // 32):
+        p = p + prod[..., k, :]
+    lanes = np.arange(32)
+    for off in (16, 8, 4, 2, 1):
+        p = p + p[..., lanes ^ off]
+    return p[..., 0]
+
+
 def cosine_scores(metric, a_idx, b_idx) -> np.ndarray:
-    """[B, Ns, Nd] fp64 cosine similarities (the build's exact contract)."""
+    """[B, Ns, Nd] fp64 cosine similarities evaluated with BLAS (for the
+    arg-max search; exact values come from ``exact_cosine``)."""
     x = to_f64(metric)
     a, b = x[:, a_idx], x[:, b_idx]
     na = np.sqrt(np.einsum("bnc,bnc->bn", a, a))
@@ -76,15 +100,40 @@ def cosine_scores(metric, a_idx, b_idx) -> np.ndarray:
     return dots / (na[:, :, None] * nb[:, None, :])
 
 
+def exact_cosine(x, bb, i, j, a_idx, b_idx) -> np.ndarray:
+    """The contract's cosine of src i and dst j of batch row bb (arrays):
+    lane_dot(a, b) / (sqrt(lane_dot(a, a)) * sqrt(lane_dot(b, b)))."""
+    a = x[bb, a_idx[i]]
+    b = x[bb, b_idx[j]]
+    return lane_dot(a, b) / (np.sqrt(lane_dot(a, a)) * np.sqrt(lane_dot(b, b)))
+
+
 def match(metric, a_idx, b_idx, r: int, scores=None):
     """Returns dict(unm_idx, src_idx, dst_idx, counter, node_max, node_idx);
-    indices are positions within a_idx / b_idx (int64)."""
+    indices are positions within a_idx / b_idx (int64).  The arg-max is over
+    the contract's exact cosines: every candidate within 1e-12 of the BLAS
+    row maximum (BLAS error is ~1e-15) is re-evaluated with ``exact_cosine``;
+    ties go to the lower dst position."""
+    x = to_f64(metric)
+    a_idx = np.asarray(a_idx)
+    b_idx = np.asarray(b_idx)
     if scores is None:
-        scores = cosine_scores(metric, a_idx, b_idx)
+        scores = cosine_scores(x, a_idx, b_idx)
     B, Ns, Nd = scores.shape
     r = min(Ns, r)
-    node_idx = np.argmax(scores, axis=-1)  # first (lowest) position among equal maxima
-    node_max = np.take_along_axis(scores, node_idx[..., None], axis=-1)[..., 0]
+    rowmax = scores.max(axis=-1)
+    bb, ii, jj = np.nonzero(scores >= rowmax[..., None] - 1e-12)
+    ex = exact_cosine(x, bb, ii, jj, a_idx, b_idx)
+    node_max = np.full((B, Ns), -np.inf)
+    node_idx = np.full((B, Ns), np.iinfo(np.int64).max, dtype=np.int64)
+    # visit candidates by (row, exact value desc, column asc): the first wins
+    order = np.lexsort((jj, -ex, ii, bb))
+    first = np.ones(order.size, dtype=bool)
+    key = bb[order] * Ns + ii[order]
+    first[1:] = key[1:] != key[:-1]
+    sel = order[first]
+    node_max[bb[sel], ii[sel]] = ex[sel]
+    node_idx[bb[sel], ii[sel]] = jj[sel]
     edge = np.argsort(-node_max, axis=-1, kind="stable")
     unm_idx, src_idx = edge[:, r:], edge[:, :r]
     dst_idx = np.take_along_axis(node_idx, src_idx, axis=-1)

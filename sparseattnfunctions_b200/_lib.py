@@ -83,6 +83,12 @@ class SelectCfg(ctypes.Structure):
     ]
 
 
+class TomePlan(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in (
+        "unm_idx", "src_idx", "dst_idx", "counter", "dst_ptr", "dst_src", "token_map", "log_count",
+        "node_max", "node_idx")]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -106,6 +112,12 @@ SIGNATURES = {
     "saf_mask_to_csr": (_I32, [_P, _I64, _I32, _I32, _I64, _I64, _P, _P, _P]),
     "saf_bsa_fwd": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I64, _F32, _I32,
                            _P]),
+    "saf_tome_match_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
+    "saf_tome_match": (_I32, [_P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I32,
+                              ctypes.POINTER(TomePlan), _P, _SZ, _P]),
+    "saf_tome_merge": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I64, _P,
+                              _I64, _I32, ctypes.POINTER(TomePlan), _P]),
+    "saf_tome_unmerge": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I64, _P, _P]),
 }
 
 _lib = None

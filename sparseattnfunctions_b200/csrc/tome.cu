@@ -1,0 +1,794 @@
+// tome.cu -- ToMe bipartite soft matching, merge and unmerge for sm_100a.
+//
+// Restates special_attentions/utils/merge_unmerge.py:34-154 on the GPU:
+//   match  (:99-116) cosine similarity of every src token with every dst
+//          token, per src the best dst (node_max, node_idx), src ordered by
+//          node_max descending, the first r merged (src_idx -> dst_idx), the
+//          rest kept (unm_idx), counter = 1 + number merged into each dst;
+//   merge  (:119-135) [unm | dst mean of itself and its merged src];
+//   unmerge (:137-154) every token reads its row of the merged sequence.
+//
+// Exact matching contract (the reference's bf16 scores are tie-dominated):
+// cos(a, b) = dot(a, b) / (sqrt(|a|^2) * sqrt(|b|^2)) in fp64 on the input
+// values with every dot product summed in one fixed order (products of
+// 16-bit values are exact in fp64; lane l of a warp adds the products of
+// columns l, l+32, ... in ascending order, then the 32 lane sums are combined
+// by an xor butterfly with offsets 16, 8, 4, 2, 1), correctly rounded
+// sqrt / mul / div; arg-max ties -> lower dst position, sort ties -> lower
+// src position.  Done in three stages so no src x dst score matrix reaches HBM:
+//   1. tensor cores (tcgen05, bf16/f16 inputs, fp32 accumulation) score every
+//      pair as s~ = dot~ * (1/|b|); each src row keeps its 8 best candidates;
+//   2. the candidates are re-scored exactly in fp64.  The fp32 accumulation
+//      error of dot~ is below eps * |a| * |b| with eps = 2^-12 (at least 15x
+//      the bound (C/16 + 16) * 2^-23 for C <= 2048), so the true best dst has
+//      s~ >= s~_top1 - 2 * eps * |a|; when the 8th candidate is below that
+//      line the exact winner is among the 8, otherwise the row is re-scanned
+//      exactly over all dst;
+//   3. a stable radix sort of node_max (descending) orders the src rows.
+#include <cub/device/device_segmented_radix_sort.cuh>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "saf_common.cuh"
+
+namespace saf {
+namespace {
+
+constexpr int kTM = 128;    // src rows per CTA
+constexpr int kTN = 256;    // dst columns per MMA tile
+constexpr int kTK = 64;     // K chunk: one 128-byte swizzle row of 16-bit values
+constexpr int kStages = 4;  // smem ring depth
+constexpr int kCand = 8;    // candidates kept per src row
+constexpr int kScoreThreads = 384;  // warp 0 TMA, warp 1 MMA, 2-3 idle, 4-11 epilogue
+constexpr double kEps = 1.0 / 4096.0;  // accumulation error bound / (|a| |b|)
+
+struct ScoreParams {
+  int B, Ns, Nd, Cp;
+  const float* rinv_b;  // [B, Nd] 1 / |b| (fp32)
+  int32_t* cand_idx;    // [B, Ns, 8]
+  float* cand_val;      // [B, Ns, 8]
+  unsigned int* status;
+  uint64_t budget_ns;
+};
+
+struct ScoreLayout {
+  static constexpr int kABytes = kTM * kTK * 2;  // 16 KB
+  static constexpr int kBBytes = kTN * kTK * 2;  // 32 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kOffRing = 0;
+  static constexpr int kOffCand = kStages * kStageBytes;            // [2][128][8] (val, idx)
+  static constexpr int kOffBar = kOffCand + 2 * kTM * kCand * 8;
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain, xend
+  static constexpr int kNumBars = 2 * kStages + 6;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kDynSmem = kOffMisc + 16 + 1024;
+};
+
+__device__ __forceinline__ void cand_insert(float (&v)[kCand], int (&ix)[kCand], float s, int j) {
+  if (!(s > v[kCand - 1])) return;
+  v[kCand - 1] = s;
+  ix[kCand - 1] = j;
+#pragma unroll
+  for (int i = kCand - 1; i > 0; --i) {
+    if (v[i] > v[i - 1]) {
+      const float tv = v[i];
+      v[i] = v[i - 1];
+      v[i - 1] = tv;
+      const int ti = ix[i];
+      ix[i] = ix[i - 1];
+      ix[i - 1] = ti;
+    }
+  }
+}
+
+// grid (ceil(Ns/128), B).  One CTA per SM (TMEM: two 256-column accumulators).
+template <bool kBF16>
+__global__ void __launch_bounds__(kScoreThreads, 1)
+    tome_score_kernel(const __grid_constant__ CUtensorMap tm_a,
+                      const __grid_constant__ CUtensorMap tm_b, const ScoreParams p) {
+  using L = ScoreLayout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kTM, b = blockIdx.y;
+  const int n_tiles = (p.Nd + kTN - 1) / kTN, k_chunks = p.Cp / kTK;
+  const uint32_t ring = smem_u32(smem + L::kOffRing);
+  const uint32_t bar0 = smem_u32(smem + L::kOffBar);
+  auto bar_full = [&](int s) { return bar0 + 8u * s; };
+  auto bar_empty = [&](int s) { return bar0 + 8u * (kStages + s); };
+  auto bar_acc_full = [&](int i) { return bar0 + 8u * (2 * kStages + i); };
+  auto bar_acc_empty = [&](int i) { return bar0 + 8u * (2 * kStages + 2 + i); };
+  const uint32_t bar_drain = bar0 + 8u * (2 * kStages + 4);
+  const uint32_t bar_xend = bar0 + 8u * (2 * kStages + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_acc_full(i), 1);
+      mbar_init(bar_acc_empty(i), 256);
+    }
+    mbar_init(bar_drain, 1);
+    mbar_init(bar_xend, 256);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int issued = 0;
+    if (lane == 0) {
+      for (int nt = 0; nt < n_tiles; ++nt) {
+        for (int kc = 0; kc < k_chunks; ++kc, ++issued) {
+          const int s = issued % kStages;
+          const uint32_t ph = (issued / kStages) & 1;
+          if (!mbar_wait(bar_empty(s), ph ^ 1, abort_flag, p.status, p.budget_ns)) break;
+          const uint32_t st = ring + s * L::kStageBytes;
+          mbar_arrive_expect_tx(bar_full(s), L::kStageBytes);
+          tma_load_3d(st, &tm_a, bar_full(s), kc * kTK, m0, b);
+          tma_load_3d(st + L::kABytes, &tm_b, bar_full(s), kc * kTK, nt * kTN, b);
+        }
+        if (*abort_flag) break;
+      }
+      // drain: wait for the last load of every stage
+      for (int s = 0; s < kStages && s < issued; ++s) {
+        const int last = s + ((issued - 1 - s) / kStages) * kStages;
+        mbar_drain(bar_full(s), (last / kStages) & 1, p.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_f16(kTM, kTN, kBF16, false, false);
+      int used = 0;
+      bool ok = true;
+      for (int nt = 0; nt < n_tiles && ok; ++nt) {
+        const int buf = nt & 1;
+        if (!mbar_wait(bar_acc_empty(buf), ((nt >> 1) & 1) ^ 1, abort_flag, p.status,
+                       p.budget_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * kTN;
+        for (int kc = 0; kc < k_chunks; ++kc, ++used) {
+          const int s = used % kStages;
+          if (!mbar_wait(bar_full(s), (used / kStages) & 1, abort_flag, p.status, p.budget_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = ring + s * L::kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kTK / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(st + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(st + L::kABytes + kk * 32, 16, 1024);
+            tc_mma_ss(acc, ad, bd, kIdesc, (kc > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(bar_empty(s));
+        }
+        if (ok) tc_commit(bar_acc_full(buf));
+      }
+      tc_commit(bar_drain);
+      mbar_drain(bar_drain, 0, p.status);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3, chalf = (warp - 4) >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const float* rinv = p.rinv_b + static_cast<int64_t>(b) * p.Nd;
+    float cv[kCand];
+    int ci[kCand];
+#pragma unroll
+    for (int i = 0; i < kCand; ++i) {
+      cv[i] = -INFINITY;
+      ci[i] = -1;
+    }
+    bool ok = true;
+    for (int nt = 0; nt < n_tiles; ++nt) {
+      const int buf = nt & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_acc_full(buf), (nt >> 1) & 1, abort_flag,
+                                              p.status, p.budget_ns))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int col0 = nt * kTN + chalf * (kTN / 2);
+#pragma unroll 1
+      for (int c = 0; c < kTN / 2 / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_addr + buf * kTN + chalf * (kTN / 2) + c * 32, r);
+        tmem_wait_ld(r);
+        if (c == kTN / 2 / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(bar_acc_empty(buf));
+        }
+        const int jc = col0 + c * 32;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = jc + e;
+          if (j < p.Nd) cand_insert(cv, ci, __uint_as_float(r[e]) * __ldg(rinv + j), j);
+        }
+      }
+    }
+    // merge the two column halves of every row
+    float2* cand = reinterpret_cast<float2*>(smem + L::kOffCand);
+#pragma unroll
+    for (int i = 0; i < kCand; ++i)
+      cand[(chalf * kTM + row) * kCand + i] = make_float2(cv[i], __int_as_float(ci[i]));
+    mbar_arrive(bar_xend);
+    const bool have = ok && __all_sync(0xffffffffu, mbar_wait(bar_xend, 0, abort_flag, p.status,
+                                                               p.budget_ns));
+    if (have && chalf == 0 && m0 + row < p.Ns && !*abort_flag) {
+#pragma unroll
+      for (int i = 0; i < kCand; ++i) {
+        const float2 o = cand[(kTM + row) * kCand + i];
+        cand_insert(cv, ci, o.x, __float_as_int(o.y));
+      }
+      const int64_t base = (static_cast<int64_t>(b) * p.Ns + m0 + row) * kCand;
+#pragma unroll
+      for (int i = 0; i < kCand; ++i) {
+        p.cand_idx[base + i] = ci[i];
+        p.cand_val[base + i] = cv[i];
+      }
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// gather + norms: one warp per gathered row.
+template <typename T>
+__device__ __forceinline__ double ld_f64(const T* p) {
+  if constexpr (sizeof(T) == 2) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) return static_cast<double>(__bfloat162float(*p));
+    else return static_cast<double>(__half2float(*p));
+  } else {
+    return static_cast<double>(*p);
+  }
+}
+
+struct GatherParams {
+  const void* metric;
+  int64_t sb, sn;  // element strides of metric [B, N, C]
+  int B, N, C, Cp;
+  const int32_t* idx;  // [n_rows] token indices
+  int n_rows;
+  void* out;           // [B, n_rows, Cp] 16-bit
+  double* sqnorm;      // [B, n_rows]
+  float* rinv;         // [B, n_rows] or null
+  unsigned int* status;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) tome_gather_kernel(const GatherParams g) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  if (warp >= g.n_rows) return;
+  int tok = g.idx[warp];
+  T* dst = static_cast<T*>(g.out) + (static_cast<int64_t>(b) * g.n_rows + warp) * g.Cp;
+  if (tok < 0 || tok >= g.N) {
+    if (lane == 0) atomicOr(g.status, SAF_DEV_BADINDEX);
+    tok = -1;
+  }
+  const T* src = static_cast<const T*>(g.metric) + static_cast<int64_t>(b) * g.sb +
+                 static_cast<int64_t>(tok < 0 ? 0 : tok) * g.sn;
+  double acc = 0.0;
+  for (int c = lane; c < g.Cp; c += 32) {
+    T v = T(0.f);
+    if (c < g.C && tok >= 0) v = src[c];
+    dst[c] = v;
+    const double d = ld_f64(&v);
+    acc = fma(d, d, acc);  // products of 16-bit values are exact in fp64
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    g.sqnorm[static_cast<int64_t>(b) * g.n_rows + warp] = acc;
+    if (g.rinv) g.rinv[static_cast<int64_t>(b) * g.n_rows + warp] = static_cast<float>(1.0 / sqrt(acc));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// exact re-score: one warp per src row.
+struct ExactParams {
+  const void* A;        // [B, Ns, Cp] 16-bit
+  const void* Bm;       // [B, Nd, Cp] 16-bit
+  const double* na;     // [B, Ns]
+  const double* nb;     // [B, Nd]
+  const int32_t* cand_idx;
+  const float* cand_val;
+  int B, Ns, Nd, Cp;
+  double* node_max;     // [B, Ns]
+  int32_t* node_idx;    // [B, Ns]
+};
+
+template <typename T>
+__device__ __forceinline__ double exact_dot(const T* a, const T* bb, int Cp, int lane) {
+  double acc = 0.0;
+  for (int c = lane; c < Cp; c += 32) acc = fma(ld_f64(a + c), ld_f64(bb + c), acc);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  return acc;  // the contract's summation order (see the file header)
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) tome_exact_kernel(const ExactParams e) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  if (i >= e.Ns) return;
+  const int64_t ri = static_cast<int64_t>(b) * e.Ns + i;
+  const T* a = static_cast<const T*>(e.A) + ri * e.Cp;
+  const double sa = __dsqrt_rn(e.na[ri]);
+  const float* cv = e.cand_val + ri * kCand;
+  const int32_t* ci = e.cand_idx + ri * kCand;
+  const double tau = 2.0 * kEps * sa;  // in units of s~ = dot * (1/|b|)
+  const bool complete = e.Nd <= kCand ||
+                        (static_cast<double>(cv[0]) - static_cast<double>(cv[kCand - 1]) > tau &&
+                         ci[kCand - 1] >= 0);
+  double best = -INFINITY;
+  int bj = 0x7fffffff;
+  auto consider = [&](int j) {
+    const T* bb = static_cast<const T*>(e.Bm) + (static_cast<int64_t>(b) * e.Nd + j) * e.Cp;
+    const double d = exact_dot(a, bb, e.Cp, lane);
+    const double cs = __ddiv_rn(d, __dmul_rn(sa, __dsqrt_rn(e.nb[static_cast<int64_t>(b) * e.Nd + j])));
+    if (cs > best || (cs == best && j < bj)) {
+      best = cs;
+      bj = j;
+    }
+  };
+  if (complete) {
+#pragma unroll 1
+    for (int k = 0; k < kCand && k < e.Nd; ++k) {
+      const int j = ci[k];
+      if (j >= 0) consider(j);
+    }
+  } else {
+#pragma unroll 1
+    for (int j = 0; j < e.Nd; ++j) consider(j);
+  }
+  if (lane == 0) {
+    e.node_max[ri] = best;
+    e.node_idx[ri] = bj;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// plan finalisation
+struct FinalParams {
+  int B, Ns, Nd, N, r;
+  const int32_t* order;        // [B, Ns] src positions sorted by node_max desc
+  const int32_t* node_idx;     // [B, Ns]
+  const int32_t* a_idx;        // [Ns]
+  const int32_t* b_idx;        // [Nd]
+  int32_t* unm_idx;            // [B, Ns - r]
+  int32_t* src_idx;            // [B, r]
+  int32_t* dst_idx;            // [B, r]
+  int32_t* dst_key;            // [B, r] (sort input: dst of the k-th merged src)
+  int32_t* dst_val;            // [B, r] (sort input: its src position)
+  int32_t* token_map;          // [B, N] or null
+};
+
+__global__ void tome_final_kernel(const FinalParams f) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+  const int64_t bo = static_cast<int64_t>(b);
+  const int unm_len = f.Ns - f.r;
+  if (k < f.Nd && f.token_map) f.token_map[bo * f.N + f.b_idx[k]] = unm_len + k;
+  if (k >= f.Ns) return;
+  const int s = f.order[bo * f.Ns + k];
+  if (k < f.r) {
+    const int d = f.node_idx[bo * f.Ns + s];
+    f.src_idx[bo * f.r + k] = s;
+    f.dst_idx[bo * f.r + k] = d;
+    f.dst_key[bo * f.r + k] = d;
+    f.dst_val[bo * f.r + k] = s;
+    if (f.token_map) f.token_map[bo * f.N + f.a_idx[s]] = unm_len + d;
+  } else {
+    f.unm_idx[bo * unm_len + (k - f.r)] = s;
+    if (f.token_map) f.token_map[bo * f.N + f.a_idx[s]] = k - f.r;
+  }
+}
+
+// dst_ptr[b, j] = first position of dst j in the dst-sorted merged list;
+// counter = 1 + count; log_count = log(counter).
+__global__ void tome_dstptr_kernel(int B, int Nd, int r, const int32_t* __restrict__ keys_sorted,
+                                   int32_t* __restrict__ dst_ptr, int32_t* __restrict__ counter,
+                                   float* __restrict__ log_count) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+  if (j > Nd) return;
+  const int32_t* kk = keys_sorted + static_cast<int64_t>(b) * r;
+  int lo = 0, hi = r;  // lower_bound(j)
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (kk[mid] < j) lo = mid + 1;
+    else hi = mid;
+  }
+  dst_ptr[static_cast<int64_t>(b) * (Nd + 1) + j] = lo;
+  if (j < Nd) {
+    int lo2 = lo, hi2 = r;  // lower_bound(j + 1)
+    while (lo2 < hi2) {
+      const int mid = (lo2 + hi2) >> 1;
+      if (kk[mid] < j + 1) lo2 = mid + 1;
+      else hi2 = mid;
+    }
+    const int c = 1 + (lo2 - lo);
+    counter[static_cast<int64_t>(b) * Nd + j] = c;
+    if (log_count) log_count[static_cast<int64_t>(b) * Nd + j] = logf(static_cast<float>(c));
+  }
+}
+
+__global__ void tome_offsets_kernel(int B, int n, int* __restrict__ off) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i <= B) off[i] = i * n;
+}
+
+__global__ void tome_iota_kernel(int B, int n, int32_t* __restrict__ v) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+  if (i < n) v[static_cast<int64_t>(b) * n + i] = i;
+}
+
+// ---------------------------------------------------------------------------
+// merge / unmerge: one warp per output row.
+struct RowCopyParams {
+  const void* x;
+  void* out;
+  int64_t x_sb, x_sn, o_sb, o_sn;  // element strides ([B, rows, C])
+  int B, C, text;                  // text rows copied unchanged
+  int Ns, Nd, r, N;
+  const int32_t* a_idx;
+  const int32_t* b_idx;
+  const int32_t* unm_idx;   // [B, Ns - r]
+  const int32_t* counter;   // [B, Nd]
+  const int32_t* dst_ptr;   // [B, Nd + 1]
+  const int32_t* dst_src;   // [B, r]
+  const int32_t* token_map; // [B, N]
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(v);
+  else if constexpr (std::is_same<T, __half>::value) return __half2float(v);
+  else return v;
+}
+template <typename T>
+__device__ __forceinline__ T from_f(float v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return __float2bfloat16_rn(v);
+  else if constexpr (std::is_same<T, __half>::value) return __float2half_rn(v);
+  else return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) tome_merge_kernel(const RowCopyParams q) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  const int unm_len = q.Ns - q.r;
+  const int out_rows = q.text + unm_len + q.Nd;
+  if (row >= out_rows) return;
+  const T* xb = static_cast<const T*>(q.x) + static_cast<int64_t>(b) * q.x_sb;
+  T* ob = static_cast<T*>(q.out) + static_cast<int64_t>(b) * q.o_sb + static_cast<int64_t>(row) * q.o_sn;
+  const int64_t bo = b;
+  if (row < q.text || row < q.text + unm_len) {
+    const int src_row = row < q.text ? row : q.text + q.a_idx[q.unm_idx[bo * unm_len + row - q.text]];
+    const T* xs = xb + static_cast<int64_t>(src_row) * q.x_sn;
+    for (int c = lane; c < q.C; c += 32) ob[c] = xs[c];
+    return;
+  }
+  // dst row: (x_dst + sum of merged src, in ascending merge order) / counter
+  const int j = row - q.text - unm_len;
+  const T* xd = xb + static_cast<int64_t>(q.text + q.b_idx[j]) * q.x_sn;
+  const int p0 = q.dst_ptr[bo * (q.Nd + 1) + j], p1 = q.dst_ptr[bo * (q.Nd + 1) + j + 1];
+  const float inv = 1.f / static_cast<float>(q.counter[bo * q.Nd + j]);
+  for (int c = lane; c < q.C; c += 32) {
+    float acc = to_f(xd[c]);
+    for (int t = p0; t < p1; ++t) {
+      const int s = q.dst_src[bo * q.r + t];
+      acc += to_f(xb[static_cast<int64_t>(q.text + q.a_idx[s]) * q.x_sn + c]);
+    }
+    ob[c] = from_f<T>(acc * inv);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) tome_unmerge_kernel(const RowCopyParams q) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  if (row >= q.text + q.N) return;
+  const int src_row = row < q.text ? row : q.text + q.token_map[static_cast<int64_t>(b) * q.N + row - q.text];
+  const T* xs = static_cast<const T*>(q.x) + static_cast<int64_t>(b) * q.x_sb + static_cast<int64_t>(src_row) * q.x_sn;
+  T* ob = static_cast<T*>(q.out) + static_cast<int64_t>(b) * q.o_sb + static_cast<int64_t>(row) * q.o_sn;
+  if ((q.C * sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(xs) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(ob) & 15) == 0) {
+    const int nv = q.C * static_cast<int>(sizeof(T)) / 16;
+    for (int c = lane; c < nv; c += 32) reinterpret_cast<uint4*>(ob)[c] = reinterpret_cast<const uint4*>(xs)[c];
+  } else {
+    for (int c = lane; c < q.C; c += 32) ob[c] = xs[c];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// workspace layout of saf_tome_match
+struct MatchLayout {
+  size_t off_a, off_b, off_na, off_nb, off_rinv, off_ci, off_cv, off_nmax, off_nidx;
+  size_t off_keys_out, off_vals_in, off_vals_out, off_dkey, off_dkey_out, off_dval_out, off_seg1,
+      off_seg2, off_cub, cub_bytes, total;
+};
+
+size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+MatchLayout match_layout(int64_t B, int64_t Ns, int64_t Nd, int64_t Cp, int64_t r) {
+  MatchLayout l{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = up256(o + bytes);
+    return at;
+  };
+  l.off_a = take(B * Ns * Cp * 2);
+  l.off_b = take(B * Nd * Cp * 2);
+  l.off_na = take(B * Ns * 8);
+  l.off_nb = take(B * Nd * 8);
+  l.off_rinv = take(B * Nd * 4);
+  l.off_ci = take(B * Ns * kCand * 4);
+  l.off_cv = take(B * Ns * kCand * 4);
+  l.off_nmax = take(B * Ns * 8);
+  l.off_nidx = take(B * Ns * 4);
+  l.off_keys_out = take(B * Ns * 8);
+  l.off_vals_in = take(B * Ns * 4);
+  l.off_vals_out = take(B * Ns * 4);
+  l.off_dkey = take(B * (r > 0 ? r : 1) * 4);
+  l.off_dkey_out = take(B * (r > 0 ? r : 1) * 4);
+  l.off_dval_out = take(B * (r > 0 ? r : 1) * 4);
+  l.off_seg1 = take((B + 1) * 4);
+  l.off_seg2 = take((B + 1) * 4);
+  // CUB temp storage: the larger of the two segmented sorts
+  size_t t1 = 0, t2 = 0;
+  cub::DeviceSegmentedRadixSort::SortPairsDescending(
+      nullptr, t1, static_cast<const double*>(nullptr), static_cast<double*>(nullptr),
+      static_cast<const int*>(nullptr), static_cast<int*>(nullptr), static_cast<int>(B * Ns),
+      static_cast<int>(B), static_cast<const int*>(nullptr), static_cast<const int*>(nullptr));
+  cub::DeviceSegmentedRadixSort::SortPairs(
+      nullptr, t2, static_cast<const int*>(nullptr), static_cast<int*>(nullptr),
+      static_cast<const int*>(nullptr), static_cast<int*>(nullptr),
+      static_cast<int>(B * (r > 0 ? r : 1)), static_cast<int>(B), static_cast<const int*>(nullptr),
+      static_cast<const int*>(nullptr));
+  l.cub_bytes = t1 > t2 ? t1 : t2;
+  l.off_cub = take(l.cub_bytes);
+  l.total = o;
+  return l;
+}
+
+int64_t pad_c(int64_t C) { return (C + kTK - 1) / kTK * kTK; }
+
+int32_t make_rows_map(CUtensorMap* map, void* base, int64_t B, int64_t rows, int64_t Cp, int box_rows,
+                      bool bf16) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(Cp), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(Cp) * 2, static_cast<cuuint64_t>(rows * Cp) * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kTK), static_cast<cuuint32_t>(box_rows), 1u};
+  const CUresult r = encode_tensor_map(
+      map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims,
+      strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  return r == CUDA_SUCCESS ? SAF_OK : SAF_ERR_STRIDE;
+}
+
+}  // namespace
+}  // namespace saf
+
+using namespace saf;
+
+extern "C" size_t saf_tome_match_workspace_bytes(int64_t B, int64_t Ns, int64_t Nd, int64_t C,
+                                                 int32_t r) {
+  if (B <= 0 || Ns <= 0 || Nd <= 0 || C <= 0) return 0;
+  return match_layout(B, Ns, Nd, pad_c(C), r < 0 ? 0 : (r > Ns ? Ns : r)).total;
+}
+
+extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, int64_t N,
+                                  int64_t C, int64_t stride_b, int64_t stride_n,
+                                  const int32_t* a_idx, int64_t Ns, const int32_t* b_idx,
+                                  int64_t Nd, int32_t r, const saf_tome_plan* plan,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (metric == nullptr || a_idx == nullptr || b_idx == nullptr || plan == nullptr) return SAF_ERR_ARG;
+  if (dtype != SAF_BF16 && dtype != SAF_F16) return SAF_ERR_DTYPE;
+  if (B <= 0 || N <= 0 || C <= 0 || Ns <= 0 || Nd <= 0 || Ns + Nd > N) return SAF_ERR_SHAPE;
+  if (B > 65535 || N >= (int64_t(1) << 30) || C > 65536) return SAF_ERR_SHAPE;
+  if (stride_n < C || stride_b < 0) return SAF_ERR_STRIDE;
+  if (r < 0) return SAF_ERR_ARG;
+  const int64_t rr = r > Ns ? Ns : r;  // "can't reduce more than the # tokens in src"
+  if (rr > 0 && (plan->src_idx == nullptr || plan->dst_idx == nullptr)) return SAF_ERR_ARG;
+  if (rr < Ns && plan->unm_idx == nullptr) return SAF_ERR_ARG;
+  if (plan->counter == nullptr || plan->dst_ptr == nullptr || plan->dst_src == nullptr)
+    return SAF_ERR_ARG;
+  const int64_t Cp = pad_c(C);
+  const MatchLayout lay = match_layout(B, Ns, Nd, Cp, rr);
+  if (workspace == nullptr || workspace_bytes < lay.total ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return SAF_ERR_WORKSPACE;
+  int32_t rc = bind_device_of(metric);
+  if (rc != SAF_OK) return rc;
+  if (!current_device_is_sm100()) return SAF_ERR_UNSUPPORTED;
+  unsigned int* status = device_status_ptr();
+  if (status == nullptr) return SAF_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* A = ws + lay.off_a;
+  void* Bm = ws + lay.off_b;
+  double* na = reinterpret_cast<double*>(ws + lay.off_na);
+  double* nb = reinterpret_cast<double*>(ws + lay.off_nb);
+  float* rinv = reinterpret_cast<float*>(ws + lay.off_rinv);
+  int32_t* ci = reinterpret_cast<int32_t*>(ws + lay.off_ci);
+  float* cv = reinterpret_cast<float*>(ws + lay.off_cv);
+  double* nmax = plan->node_max ? plan->node_max : reinterpret_cast<double*>(ws + lay.off_nmax);
+  int32_t* nidx = plan->node_idx ? plan->node_idx : reinterpret_cast<int32_t*>(ws + lay.off_nidx);
+  const bool bf16 = dtype == SAF_BF16;
+
+  // 1. gather src / dst rows (zero-padded to Cp) and their exact norms
+  GatherParams g{metric, stride_b, stride_n, static_cast<int>(B), static_cast<int>(N),
+                 static_cast<int>(C), static_cast<int>(Cp), a_idx, static_cast<int>(Ns), A, na,
+                 nullptr, status};
+  dim3 gg_a(static_cast<unsigned>((Ns + 7) / 8), static_cast<unsigned>(B));
+  GatherParams gb = g;
+  gb.idx = b_idx;
+  gb.n_rows = static_cast<int>(Nd);
+  gb.out = Bm;
+  gb.sqnorm = nb;
+  gb.rinv = rinv;
+  dim3 gg_b(static_cast<unsigned>((Nd + 7) / 8), static_cast<unsigned>(B));
+  if (bf16) {
+    tome_gather_kernel<__nv_bfloat16><<<gg_a, 256, 0, st>>>(g);
+    tome_gather_kernel<__nv_bfloat16><<<gg_b, 256, 0, st>>>(gb);
+  } else {
+    tome_gather_kernel<__half><<<gg_a, 256, 0, st>>>(g);
+    tome_gather_kernel<__half><<<gg_b, 256, 0, st>>>(gb);
+  }
+  SAF_CUDA_TRY(cudaGetLastError());
+
+  // 2. tensor-core scores with the top-8 epilogue
+  CUtensorMap ma, mb;
+  if ((rc = make_rows_map(&ma, A, B, Ns, Cp, kTM, bf16)) != SAF_OK) return rc;
+  if ((rc = make_rows_map(&mb, Bm, B, Nd, Cp, kTN, bf16)) != SAF_OK) return rc;
+  ScoreParams sp{static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd), static_cast<int>(Cp),
+                 rinv, ci, cv, status, wait_budget_ns()};
+  dim3 sg(static_cast<unsigned>((Ns + kTM - 1) / kTM), static_cast<unsigned>(B));
+  const int smem = ScoreLayout::kDynSmem;
+  if (bf16) {
+    SAF_CUDA_TRY(cudaFuncSetAttribute(tome_score_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    tome_score_kernel<true><<<sg, kScoreThreads, smem, st>>>(ma, mb, sp);
+  } else {
+    SAF_CUDA_TRY(cudaFuncSetAttribute(tome_score_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    tome_score_kernel<false><<<sg, kScoreThreads, smem, st>>>(ma, mb, sp);
+  }
+  SAF_CUDA_TRY(cudaGetLastError());
+
+  // 3. exact fp64 re-score of the candidates
+  ExactParams ep{A, Bm, na, nb, ci, cv, static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd),
+                 static_cast<int>(Cp), nmax, nidx};
+  if (bf16) tome_exact_kernel<__nv_bfloat16><<<gg_a, 256, 0, st>>>(ep);
+  else tome_exact_kernel<__half><<<gg_a, 256, 0, st>>>(ep);
+  SAF_CUDA_TRY(cudaGetLastError());
+
+  // 4. stable sort of node_max (descending) per batch row
+  int* seg1 = reinterpret_cast<int*>(ws + lay.off_seg1);
+  int* seg2 = reinterpret_cast<int*>(ws + lay.off_seg2);
+  int32_t* vals_in = reinterpret_cast<int32_t*>(ws + lay.off_vals_in);
+  int32_t* order = reinterpret_cast<int32_t*>(ws + lay.off_vals_out);
+  double* keys_out = reinterpret_cast<double*>(ws + lay.off_keys_out);
+  tome_offsets_kernel<<<static_cast<unsigned>((B + 256) / 256), 256, 0, st>>>(static_cast<int>(B), static_cast<int>(Ns), seg1);
+  tome_iota_kernel<<<dim3(static_cast<unsigned>((Ns + 255) / 256), static_cast<unsigned>(B)), 256, 0, st>>>(
+      static_cast<int>(B), static_cast<int>(Ns), vals_in);
+  size_t tb = lay.cub_bytes;
+  SAF_CUDA_TRY(cub::DeviceSegmentedRadixSort::SortPairsDescending(
+      ws + lay.off_cub, tb, nmax, keys_out, vals_in, order, static_cast<int>(B * Ns),
+      static_cast<int>(B), seg1, seg1 + 1, 0, 64, st));
+
+  // 5. plan: src / dst / unm indices, token map, dst -> src lists, counters
+  int32_t* dkey = reinterpret_cast<int32_t*>(ws + lay.off_dkey);
+  int32_t* dkey_out = reinterpret_cast<int32_t*>(ws + lay.off_dkey_out);
+  FinalParams fp{static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd), static_cast<int>(N),
+                 static_cast<int>(rr), order, nidx, a_idx, b_idx, plan->unm_idx, plan->src_idx,
+                 plan->dst_idx, dkey, reinterpret_cast<int32_t*>(ws + lay.off_dval_out), plan->token_map};
+  const int64_t nmax_k = Ns > Nd ? Ns : Nd;
+  tome_final_kernel<<<dim3(static_cast<unsigned>((nmax_k + 255) / 256), static_cast<unsigned>(B)), 256, 0, st>>>(fp);
+  SAF_CUDA_TRY(cudaGetLastError());
+  if (rr > 0) {
+    tome_offsets_kernel<<<static_cast<unsigned>((B + 256) / 256), 256, 0, st>>>(static_cast<int>(B), static_cast<int>(rr), seg2);
+    size_t tb2 = lay.cub_bytes;
+    SAF_CUDA_TRY(cub::DeviceSegmentedRadixSort::SortPairs(
+        ws + lay.off_cub, tb2, dkey, dkey_out, reinterpret_cast<int32_t*>(ws + lay.off_dval_out),
+        plan->dst_src, static_cast<int>(B * rr), static_cast<int>(B), seg2, seg2 + 1, 0, 32, st));
+  }
+  tome_dstptr_kernel<<<dim3(static_cast<unsigned>((Nd + 1 + 255) / 256), static_cast<unsigned>(B)), 256, 0, st>>>(
+      static_cast<int>(B), static_cast<int>(Nd), static_cast<int>(rr), dkey_out, plan->dst_ptr,
+      plan->counter, plan->log_count);
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}
+
+namespace {
+int32_t check_rows(const void* p, int32_t dtype) {
+  if (p == nullptr) return SAF_ERR_ARG;
+  if (dtype != SAF_BF16 && dtype != SAF_F16 && dtype != SAF_F32) return SAF_ERR_DTYPE;
+  return SAF_OK;
+}
+}  // namespace
+
+extern "C" int32_t saf_tome_merge(const void* x, void* out, int32_t dtype, int64_t B, int64_t C,
+                                  int64_t x_stride_b, int64_t x_stride_n, int64_t o_stride_b,
+                                  int64_t o_stride_n, int32_t text_len, const int32_t* a_idx,
+                                  int64_t Ns, const int32_t* b_idx, int64_t Nd, int32_t r,
+                                  const saf_tome_plan* plan, void* stream) {
+  int32_t rc;
+  if ((rc = check_rows(x, dtype)) != SAF_OK || (rc = check_rows(out, dtype)) != SAF_OK) return rc;
+  if (plan == nullptr || a_idx == nullptr || b_idx == nullptr || plan->counter == nullptr ||
+      plan->dst_ptr == nullptr || plan->dst_src == nullptr)
+    return SAF_ERR_ARG;
+  if (B <= 0 || C <= 0 || Ns <= 0 || Nd <= 0 || text_len < 0 || r < 0 || r > Ns || B > 65535)
+    return SAF_ERR_SHAPE;
+  if (r < Ns && plan->unm_idx == nullptr) return SAF_ERR_ARG;
+  if (x_stride_n < C || o_stride_n < C) return SAF_ERR_STRIDE;
+  if ((rc = bind_device_of(x)) != SAF_OK) return rc;
+  RowCopyParams q{x, out, x_stride_b, x_stride_n, o_stride_b, o_stride_n, static_cast<int>(B),
+                  static_cast<int>(C), text_len, static_cast<int>(Ns), static_cast<int>(Nd), r, 0,
+                  a_idx, b_idx, plan->unm_idx, plan->counter, plan->dst_ptr, plan->dst_src, nullptr};
+  const int64_t rows = text_len + (Ns - r) + Nd;
+  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(B));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SAF_BF16: tome_merge_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(q); break;
+    case SAF_F16: tome_merge_kernel<__half><<<grid, 256, 0, st>>>(q); break;
+    default: tome_merge_kernel<float><<<grid, 256, 0, st>>>(q); break;
+  }
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}
+
+extern "C" int32_t saf_tome_unmerge(const void* y, void* out, int32_t dtype, int64_t B, int64_t C,
+                                    int64_t y_stride_b, int64_t y_stride_n, int64_t o_stride_b,
+                                    int64_t o_stride_n, int32_t text_len, int64_t N,
+                                    const int32_t* token_map, void* stream) {
+  int32_t rc;
+  if ((rc = check_rows(y, dtype)) != SAF_OK || (rc = check_rows(out, dtype)) != SAF_OK) return rc;
+  if (token_map == nullptr) return SAF_ERR_ARG;
+  if (B <= 0 || C <= 0 || N <= 0 || text_len < 0 || B > 65535) return SAF_ERR_SHAPE;
+  if (y_stride_n < C || o_stride_n < C) return SAF_ERR_STRIDE;
+  if ((rc = bind_device_of(y)) != SAF_OK) return rc;
+  RowCopyParams q{y, out, y_stride_b, y_stride_n, o_stride_b, o_stride_n, static_cast<int>(B),
+                  static_cast<int>(C), text_len, 0, 0, 0, static_cast<int>(N), nullptr, nullptr,
+                  nullptr, nullptr, nullptr, nullptr, token_map};
+  const int64_t rows = text_len + N;
+  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(B));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SAF_BF16: tome_unmerge_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(q); break;
+    case SAF_F16: tome_unmerge_kernel<__half><<<grid, 256, 0, st>>>(q); break;
+    default: tome_unmerge_kernel<float><<<grid, 256, 0, st>>>(q); break;
+  }
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}

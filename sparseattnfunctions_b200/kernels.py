@@ -209,3 +209,131 @@ def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm
                                      _stream_ptr(dev))
     _lib.check("saf_bsa_fwd", rc)
     return out
+
+
+# --------------------------------------------------------------------------- ToMe
+
+@dataclass
+class TomePlan:
+    """Result of a bipartite matching (see ``saf_tome_plan`` in saf_api.h).
+
+    Positions refer to ``a_idx`` (src, length Ns) and ``b_idx`` (dst, length
+    Nd), the video-token indices of the split.  ``token_map[b, t]`` is the row
+    of the merged video sequence ``[unm | dst]`` that token ``t`` reads back
+    on unmerge."""
+
+    a_idx: torch.Tensor
+    b_idx: torch.Tensor
+    unm_idx: torch.Tensor
+    src_idx: torch.Tensor
+    dst_idx: torch.Tensor
+    counter: torch.Tensor
+    dst_ptr: torch.Tensor
+    dst_src: torch.Tensor
+    token_map: torch.Tensor
+    log_count: torch.Tensor
+    node_max: Optional[torch.Tensor]
+    node_idx: Optional[torch.Tensor]
+    B: int
+    N: int
+    r: int
+
+    @property
+    def Ns(self) -> int:
+        return self.a_idx.numel()
+
+    @property
+    def Nd(self) -> int:
+        return self.b_idx.numel()
+
+    @property
+    def merged_len(self) -> int:
+        return self.Ns - self.r + self.Nd
+
+    def _struct(self) -> _lib.TomePlan:
+        ptr = lambda t: None if t is None else t.data_ptr()
+        return _lib.TomePlan(ptr(self.unm_idx), ptr(self.src_idx), ptr(self.dst_idx),
+                             ptr(self.counter), ptr(self.dst_ptr), ptr(self.dst_src),
+                             ptr(self.token_map), ptr(self.log_count), ptr(self.node_max),
+                             ptr(self.node_idx))
+
+
+_T16 = {torch.bfloat16: _lib.SAF_BF16, torch.float16: _lib.SAF_F16}
+
+
+def tome_match(metric: torch.Tensor, a_idx: torch.Tensor, b_idx: torch.Tensor, r: int,
+               keep_node: bool = False) -> TomePlan:
+    """Bipartite soft matching of ``metric [B, N, C]`` (bf16/f16, CUDA) between
+    the src tokens ``a_idx`` and dst tokens ``b_idx`` (int32/int64 video-token
+    indices on the same device); merges ``min(r, Ns)`` src tokens."""
+    dev = _require_cuda(metric, a_idx, b_idx)
+    if metric.dim() != 3 or metric.dtype not in _T16:
+        raise ValueError("metric must be a bf16/f16 [B, N, C] CUDA tensor")
+    if metric.stride(-1) != 1:
+        metric = metric.contiguous()
+    B, N, C = metric.shape
+    a = a_idx.to(device=dev, dtype=torch.int32).contiguous().reshape(-1)
+    b = b_idx.to(device=dev, dtype=torch.int32).contiguous().reshape(-1)
+    Ns, Nd = a.numel(), b.numel()
+    r = max(0, min(int(r), Ns))
+    i32 = dict(dtype=torch.int32, device=dev)
+    plan = TomePlan(
+        a, b, torch.empty(B, Ns - r, **i32), torch.empty(B, r, **i32), torch.empty(B, r, **i32),
+        torch.empty(B, Nd, **i32), torch.empty(B, Nd + 1, **i32), torch.empty(B, max(r, 1), **i32),
+        torch.empty(B, N, **i32), torch.empty(B, Nd, dtype=torch.float32, device=dev),
+        torch.empty(B, Ns, dtype=torch.float64, device=dev) if keep_node else None,
+        torch.empty(B, Ns, **i32) if keep_node else None, B, N, r)
+    lib = _lib.load()
+    ws_bytes = lib.saf_tome_match_workspace_bytes(B, Ns, Nd, C, r)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    st = plan._struct()
+    with torch.cuda.device(dev):
+        rc = lib.saf_tome_match(metric.data_ptr(), _T16[metric.dtype], B, N, C, metric.stride(0),
+                                metric.stride(1), a.data_ptr(), Ns, b.data_ptr(), Nd, r,
+                                ctypes.byref(st), ws.data_ptr(), ws.numel(), _stream_ptr(dev))
+    _lib.check("saf_tome_match", rc)
+    return plan
+
+
+def _rows3(x: torch.Tensor, B: int) -> torch.Tensor:
+    """[B, rows, C] view of x; a 4-D [b, h, S, D] tensor with b*h == B is
+    read as [b*h, S, D] (the per-head matching of MergeAttention)."""
+    if x.dim() == 4 and x.shape[0] * x.shape[1] == B:
+        x = x.reshape(B, x.shape[2], x.shape[3])
+    if x.dim() != 3 or x.shape[0] != B:
+        raise ValueError(f"tensor of shape {tuple(x.shape)} does not match the plan's batch {B}")
+    return x if x.stride(-1) == 1 else x.contiguous()
+
+
+def tome_merge(x: torch.Tensor, plan: TomePlan, text_len: int = 0) -> torch.Tensor:
+    """``x [B, text_len + N, C]`` -> ``[B, text_len + Ns - r + Nd, C]``."""
+    dev = _require_cuda(x)
+    x = _rows3(x, plan.B)
+    if x.shape[1] != text_len + plan.N:
+        raise ValueError(f"x has {x.shape[1]} rows, expected text_len + N = {text_len + plan.N}")
+    out = torch.empty(plan.B, text_len + plan.merged_len, x.shape[-1], dtype=x.dtype, device=dev)
+    st = plan._struct()
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_tome_merge(x.data_ptr(), out.data_ptr(), _DTYPES[x.dtype], plan.B,
+                                        x.shape[-1], x.stride(0), x.stride(1), out.stride(0),
+                                        out.stride(1), text_len, plan.a_idx.data_ptr(), plan.Ns,
+                                        plan.b_idx.data_ptr(), plan.Nd, plan.r, ctypes.byref(st),
+                                        _stream_ptr(dev))
+    _lib.check("saf_tome_merge", rc)
+    return out
+
+
+def tome_unmerge(y: torch.Tensor, plan: TomePlan, text_len: int = 0) -> torch.Tensor:
+    """``y [B, text_len + Ns - r + Nd, C]`` -> ``[B, text_len + N, C]``."""
+    dev = _require_cuda(y)
+    y = _rows3(y, plan.B)
+    if y.shape[1] != text_len + plan.merged_len:
+        raise ValueError(f"y has {y.shape[1]} rows, expected {text_len + plan.merged_len}")
+    out = torch.empty(plan.B, text_len + plan.N, y.shape[-1], dtype=y.dtype, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_tome_unmerge(y.data_ptr(), out.data_ptr(), _DTYPES[y.dtype], plan.B,
+                                          y.shape[-1], y.stride(0), y.stride(1), out.stride(0),
+                                          out.stride(1), text_len, plan.N,
+                                          plan.token_map.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_tome_unmerge", rc)
+    return out

@@ -333,7 +333,82 @@ def run_saf(args, world, rank, local):
                          "traffic": traffic,
                          "algorithmic_flop_per_launch": live_flops},
         }
+    if not args.no_merge:
+        merge = bench_merge(args, dev, world, rank)
+        if line is not None:
+            line["merge"] = merge
     return line, (q_c, k_c, v_c), csr, cfg
+
+
+def bench_merge(args, dev, world, rank):
+    """ToMe on CogVideoX-2B hidden states [2, 17550, 1920]
+    bf16, alternate split (src even / dst odd), r = 4000; then dense
+    attention (H = 30, D = 64) over the 226 text + 13550 merged tokens with
+    the log(size) bias, and unmerge.  'ms/merge' = match + merge."""
+    import torch
+
+    from sparseattnfunctions_b200 import kernels, workloads
+    from sparseattnfunctions_b200.geometry import COGVIDEOX_2B as geo
+    from sparseattnfunctions_b200.special_attentions.utils.merge_unmerge import alternate_split
+
+    B, C, r, H, D, T = 2, 1920, 4000, 30, 64, geo.text_len
+    N = geo.video_len
+    x = workloads.video_hidden(geo, B=B, C=C, seed=4321 + rank).to(dev)
+    g = torch.Generator().manual_seed(77 + rank)
+    text = torch.randn(B, T, C, generator=g).to(torch.bfloat16).to(dev)
+    xt = torch.cat([text, x], dim=1)
+    a_idx, b_idx = alternate_split(N, dev)
+    L = T + (a_idx.numel() - r) + b_idx.numel()
+    nb = math.ceil(L / 128)
+    csr = kernels.mask_to_csr(torch.ones(B, H, nb, nb, dtype=torch.bool, device=dev), 128, 128)
+    stream = torch.cuda.current_stream(dev)
+    n = max(3, min(args.merge_steps, args.steps))
+
+    def one(ev):
+        ev[0].record(stream)
+        plan = kernels.tome_match(x, a_idx, b_idx, r)
+        ev[1].record(stream)
+        merged = kernels.tome_merge(xt, plan, text_len=T)
+        ev[2].record(stream)
+        qkv = merged.view(B, L, H, D).transpose(1, 2)
+        bias = torch.zeros(B * H, L, dtype=torch.float32, device=dev)
+        bias.view(B, H, L)[:, :, L - plan.Nd:] = plan.log_count[:, None, :]
+        ev[3].record(stream)
+        o = kernels.bsa_fwd(qkv, qkv, qkv, csr, 1.0 / math.sqrt(D), kv_bias=bias)
+        ev[4].record(stream)
+        y = kernels.tome_unmerge(o.transpose(1, 2).reshape(B, L, C), plan, text_len=T)
+        ev[5].record(stream)
+        return plan, y
+
+    mk = lambda: [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for _ in range(2):
+        one(mk())
+    torch.cuda.synchronize()
+    evs = [mk() for _ in range(n)]
+    barrier(world)
+    for e in evs:
+        plan, _ = one(e)
+    torch.cuda.synchronize()
+    avg = lambda a, b: sum(e[a].elapsed_time(e[b]) for e in evs) / n
+    m_match, m_merge, m_attn, m_unmerge = avg(0, 1), avg(1, 2), avg(3, 4), avg(4, 5)
+    m_match = allreduce(m_match, "max", world)
+    m_merge = allreduce(m_merge, "max", world)
+    gemm_flop = 2.0 * B * a_idx.numel() * b_idx.numel() * C
+    attn_flop = 4.0 * B * H * L * L * D
+    merge_bytes = (B * N * C + B * (L - T) * C) * 2
+    peaks, kind = load_peaks()
+    return {
+        "workload": "config3: ToMe r=4000 on [2,17550,1920] bf16 (alternate split), dense attention "
+                    "over 226+13550 tokens, unmerge",
+        "ms_per_merge": round(m_match + m_merge, 4), "ms_match": round(m_match, 4),
+        "ms_merge": round(m_merge, 4), "ms_attention_merged": round(m_attn, 4),
+        "ms_unmerge": round(m_unmerge, 4), "steps": n,
+        "match_gemm_tflops": round(gemm_flop / (m_match * 1e-3) / 1e12, 1),
+        "match_gemm_frac": round(gemm_flop / (m_match * 1e-3) / 1e12 / peaks["bf16_tflops"], 3),
+        "merge_gbs": round(merge_bytes / (m_merge * 1e-3) / 1e9, 1),
+        "attention_merged_tflops": round(attn_flop / (m_attn * 1e-3) / 1e12, 1),
+        "merged_tokens": L, "max_merged_size": int(plan.counter.max()),
+    }
 
 
 def run_reference(args, world, rank):
@@ -396,6 +471,8 @@ def main():
     ap.add_argument("--ref-heads", type=int, default=1, help="heads per step of the reference arm")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-merge", action="store_true", help="skip the config-3 ToMe sub-benchmark")
+    ap.add_argument("--merge-steps", type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -337,6 +337,14 @@ def run_saf(args, world, rank, local):
         merge = bench_merge(args, dev, world, rank)
         if line is not None:
             line["merge"] = merge
+    if not args.no_combined:
+        combined = bench_combined(args, dev, world, rank)
+        if line is not None:
+            line["combined"] = combined
+    if not args.no_long:
+        long_run = bench_long(args, dev, world, rank)
+        if line is not None:
+            line["long"] = long_run
     return line, (q_c, k_c, v_c), csr, cfg
 
 
@@ -364,19 +372,25 @@ def bench_merge(args, dev, world, rank):
     stream = torch.cuda.current_stream(dev)
     n = max(3, min(args.merge_steps, args.steps))
 
+    # outputs allocated once: the timed loop makes no allocation
+    merged = torch.empty(B, L, C, dtype=xt.dtype, device=dev)
+    o_rows = torch.empty(B, L, C, dtype=xt.dtype, device=dev)  # [B, L, H*D]: heads side by side
+    y = torch.empty(B, T + N, C, dtype=xt.dtype, device=dev)
+    bias = torch.zeros(B * H, L, dtype=torch.float32, device=dev)
+
     def one(ev):
         ev[0].record(stream)
         plan = kernels.tome_match(x, a_idx, b_idx, r)
         ev[1].record(stream)
-        merged = kernels.tome_merge(xt, plan, text_len=T)
+        kernels.tome_merge(xt, plan, text_len=T, out=merged)
         ev[2].record(stream)
         qkv = merged.view(B, L, H, D).transpose(1, 2)
-        bias = torch.zeros(B * H, L, dtype=torch.float32, device=dev)
         bias.view(B, H, L)[:, :, L - plan.Nd:] = plan.log_count[:, None, :]
         ev[3].record(stream)
-        o = kernels.bsa_fwd(qkv, qkv, qkv, csr, 1.0 / math.sqrt(D), kv_bias=bias)
+        kernels.bsa_fwd(qkv, qkv, qkv, csr, 1.0 / math.sqrt(D), kv_bias=bias,
+                        out=o_rows.view(B, L, H, D).transpose(1, 2))
         ev[4].record(stream)
-        y = kernels.tome_unmerge(o.transpose(1, 2).reshape(B, L, C), plan, text_len=T)
+        kernels.tome_unmerge(o_rows, plan, text_len=T, out=y)
         ev[5].record(stream)
         return plan, y
 
@@ -408,6 +422,143 @@ def bench_merge(args, dev, world, rank):
         "merge_gbs": round(merge_bytes / (m_merge * 1e-3) / 1e9, 1),
         "attention_merged_tflops": round(attn_flop / (m_attn * 1e-3) / 1e12, 1),
         "merged_tokens": L, "max_merged_size": int(plan.counter.max()),
+    }
+
+
+def bench_combined(args, dev, world, rank):
+    """combined attention (ToMe r = 4000 per (b, h) on the
+    [k, |k|, v, |v|] metric -> top-15% block selection on the merged
+    sequence -> block-sparse attention with the log(size) bias -> unmerge)
+    in all 30 layers of a random-init CogVideoX-2B-shaped block stack
+    (hidden 1920 = 30 heads x 64, B = 2, S = 17776, bf16).  Each layer
+    projects the hidden state to q / k / v (cuBLAS, outside the timed
+    region), calls the processor (timed with CUDA events), projects the
+    output back and adds it to the residual stream.  Reported: attention ms
+    per denoising step (sum over the 30 layers)."""
+    import torch
+
+    from sparseattnfunctions_b200 import workloads
+    from sparseattnfunctions_b200.geometry import COGVIDEOX_2B as geo
+    from sparseattnfunctions_b200.special_attentions.combined_attn import CombinedAttn
+
+    B, C, H, D, layers, T = 2, 1920, 30, 64, 30, geo.text_len
+    S = geo.seq_len
+    g = torch.Generator().manual_seed(99 + rank)
+    text = torch.randn(B, T, C, generator=g).to(torch.bfloat16)
+    x0 = torch.cat([text, workloads.video_hidden(geo, B=B, C=C, seed=5151 + rank)], dim=1).to(dev)
+    gd = torch.Generator(device=dev).manual_seed(2024 + rank)
+    w_qkv = [torch.randn(C, 3 * C, generator=gd, device=dev, dtype=torch.bfloat16) / math.sqrt(C)
+             for _ in range(layers)]
+    w_o = [torch.randn(C, C, generator=gd, device=dev, dtype=torch.bfloat16) * (0.5 / math.sqrt(C))
+           for _ in range(layers)]
+    attn = CombinedAttn(warmup_epoch=0, layer_num=layers, density=0.15, block_size=128, full_merge=True)
+    stream = torch.cuda.current_stream(dev)
+
+    def one_step(evs, flops=None):
+        x = x0.clone()
+        for l in range(layers):
+            qkv = (x @ w_qkv[l]).view(B, S, 3, H, D).permute(2, 0, 3, 1, 4).contiguous()
+            q, k, v = qkv[0], qkv[1], qkv[2]
+            evs[l][0].record(stream)
+            o = attn(q, k, v)
+            evs[l][1].record(stream)
+            if flops is not None:
+                L = attn._layers[l].merge_fn.plan.merged_len + T
+                flops.append(attn.last_csr.live_flops(L, L, D))
+            x = x + o.transpose(1, 2).reshape(B, S, C) @ w_o[l]
+        return x
+
+    mk = lambda: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(layers)]
+    flops = []
+    one_step(mk(), flops)  # warm-up step (also builds every layer's plan once)
+    torch.cuda.synchronize()
+    live = float(sum(float(f) for f in flops))
+    n = max(1, args.combined_steps)
+    runs = [mk() for _ in range(n)]
+    barrier(world)
+    for evs in runs:
+        one_step(evs)
+    torch.cuda.synchronize()
+    per_step = [sum(a.elapsed_time(b) for a, b in evs) for evs in runs]
+    ms = allreduce(statistics.mean(per_step), "max", world)
+    return {
+        "workload": "config4: CombinedAttn (ToMe r=4000 per (b,h), 15% blocks of 128 on the merged "
+                    "sequence, log-size bias, unmerge) in 30 layers, B=2, S=17776, H=30, D=64, bf16; "
+                    "random-init 1920-wide projections outside the timed region",
+        "ms_attention_per_step": round(ms, 3), "ms_per_layer": round(ms / layers, 4), "steps": n,
+        "merged_len": int(attn._layers[0].merge_fn.plan.merged_len + T),
+        "live_tflop_per_step": round(live / 1e12, 4),
+        "effective_tflops": round(live / (ms * 1e-3) / 1e12, 1),
+    }
+
+
+def bench_long(args, dev, world, rank):
+    """long video (25 x 30 x 45 + 226 text, S = 33976),
+    B = 2, H = 30, D = 64, bf16, 10% of 128-blocks.  Every rank holds a
+    sequence shard [B, S/N, H, D] of q / k / v; UlyssesAttention packs it,
+    exchanges it with one NCCL all-to-all (heads split 4,4,4,4,4,4,3,3 at
+    N = 8), selects blocks and runs the block-sparse kernel on its heads, and
+    sends the output rows back (second all-to-all).  Strong scaling: the
+    layer is fixed, N GPUs share it."""
+    import torch
+
+    from sparseattnfunctions_b200 import kernels, workloads
+    from sparseattnfunctions_b200.geometry import COGVIDEOX_2B_LONG as geo
+    from sparseattnfunctions_b200.special_attentions.block_mask_attn import BlockSparseAttention
+    from sparseattnfunctions_b200.ulysses import UlyssesAttention
+
+    B, H, D, S = 2, 30, 64, geo.seq_len
+    lens = [S // world + (1 if r < S % world else 0) for r in range(world)]
+    at = sum(lens[:rank])
+    full = workloads.video_qkv(geo, B=B, H=H, D=D, dtype=torch.bfloat16, seed=777)
+    q, k, v = (t.transpose(1, 2)[:, at:at + lens[rank]].contiguous().to(dev) for t in full)
+    del full
+    inner = BlockSparseAttention(block_size=128, density=0.10, geometry=geo)
+    ua = UlyssesAttention(inner, heads=H, seq_lens=lens)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        ua(q, k, v)
+    torch.cuda.synchronize()
+    h = ua.local_heads
+    live = float(inner.last_csr.live_flops(S, S, D)) if h > 0 else 0.0
+    live_total = allreduce(live, "sum", world)
+    n = max(3, min(args.long_steps, args.steps))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    barrier(world)
+    for e in evs:
+        e[0].record(stream)
+        ua(q, k, v)
+        e[1].record(stream)
+    torch.cuda.synchronize()
+    ms = allreduce(statistics.mean(a.elapsed_time(b) for a, b in evs), "max", world)
+    # the same attention on the rank's heads without the exchange
+    grid = torch.empty(S, B, 3, max(h, 1), D, dtype=torch.bfloat16, device=dev)
+    qh, kh, vh = (grid[:, :, t, :h].permute(1, 2, 0, 3) for t in range(3))
+    aev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    if h > 0:
+        torch.manual_seed(5)
+        grid.normal_()
+        for _ in range(2):
+            inner(qh, kh, vh)
+        for e in aev:
+            e[0].record(stream)
+            inner(qh, kh, vh)
+            e[1].record(stream)
+        torch.cuda.synchronize()
+        ms_attn_local = statistics.mean(a.elapsed_time(b) for a, b in aev)
+    else:
+        ms_attn_local = 0.0
+    ms_attn = allreduce(ms_attn_local, "max", world)
+    a2a_bytes = 2 * (B * lens[rank] * 3 * H * D + B * lens[rank] * H * D) * (world - 1) / max(world, 1)
+    return {
+        "workload": "config5: S=33976 (25x30x45 + 226 text), B=2, H=30, D=64, bf16, 10% of 128-blocks; "
+                    f"sequence-sharded over {world} GPU(s), Ulysses all-to-all (NCCL) to "
+                    f"{kernels.head_split(H, world)} head ranges and back",
+        "ms_per_layer": round(ms, 4), "ms_attention_only": round(ms_attn, 4),
+        "live_tflop": round(live_total / 1e12, 4),
+        "effective_tflops": round(live_total / (ms * 1e-3) / 1e12, 1),
+        "a2a_bytes_per_rank": int(a2a_bytes), "scaling": "strong", "steps": n,
     }
 
 
@@ -473,6 +624,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-merge", action="store_true", help="skip the config-3 ToMe sub-benchmark")
     ap.add_argument("--merge-steps", type=int, default=20)
+    ap.add_argument("--no-combined", action="store_true", help="skip the config-4 combined sub-benchmark")
+    ap.add_argument("--combined-steps", type=int, default=2)
+    ap.add_argument("--no-long", action="store_true", help="skip the config-5 sequence-sharded sub-benchmark")
+    ap.add_argument("--long-steps", type=int, default=10)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -150,6 +150,19 @@ int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor
                     const float* kv_bias, int64_t kv_bias_stride_bh, float sm_scale,
                     int32_t lead_rows, void* stream);
 
+/* saf_bsa_fwd with per-query-row key intervals: row_ranges (nullable,
+ * 16-byte aligned int32 [Sq, 4], shared by every head) limits the keys of
+ * query row r to [x, y) U [z, w); keys outside are masked like keys past
+ * Sk.  The CSR must list every block that some row of the query block can
+ * see (a superset is fine).  Not combinable with kv_bias.
+ * Replaces: the frame-band masks of SmartAttention.attention_with_mask and
+ * its flex_attention block mask (SmartAttention.py:30-43,130-151). */
+int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                           const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
+                           int64_t col_capacity, int32_t block_m, int32_t block_n,
+                           const float* kv_bias, int64_t kv_bias_stride_bh, float sm_scale,
+                           int32_t lead_rows, const int32_t* row_ranges, void* stream);
+
 /* ---- (3) ToMe token merging -----------------------------------------
  * Output buffers of a bipartite matching.  Positions refer to the src list
  * a_idx (length Ns) and the dst list b_idx (length Nd) of video tokens.
@@ -191,6 +204,18 @@ int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, int64_t N, 
                        const int32_t* b_idx, int64_t Nd, int32_t r, const saf_tome_plan* plan,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* The matching metric of MergeAttention: for every (b, h) and video token
+ * n (rows text_len.. of k / v [B, H, S, D], bf16 / f16), out[b*H + h, n] =
+ * [k, |k|, v, |v|] (2D + 2 values, contiguous [B*H, S - text_len, 2D + 2]);
+ * D even, at most 128.  Each norm is the fp64 sqrt of an fp64 sum of
+ * squares in a fixed order (lane l of a warp sums the pairs
+ * x[2w]^2 + x[2w+1]^2 of words w = l, l + 32 in ascending order, the lanes
+ * combine by the xor butterfly 16, 8, 4, 2, 1), rounded once to the 16-bit
+ * type.
+ * Replaces: the metric of MergeAttention.forward (MergeAttention.py:26-31). */
+int32_t saf_tome_kv_metric(const saf_tensor4* k, const saf_tensor4* v, int32_t text_len, void* out,
+                           void* stream);
+
 /* merge: x [B, text_len + N, C] -> out [B, text_len + (Ns-r) + Nd, C]:
  * text rows copied, then the kept src tokens (unm_idx order), then every dst
  * token averaged with the src merged into it (fp32 sum in edge order /
@@ -209,6 +234,36 @@ int32_t saf_tome_unmerge(const void* y, void* out, int32_t dtype, int64_t B, int
                          int64_t y_stride_b, int64_t y_stride_n, int64_t o_stride_b,
                          int64_t o_stride_n, int32_t text_len, int64_t N, const int32_t* token_map,
                          void* stream);
+
+/* Token permutation of [B, H, S, D] tensors (element strides, D
+ * contiguous): out[g, s, :] = x[g, perm[s], :] for the flat heads
+ * g = b*H + h listed in heads[0..n_heads) (every head when heads is null).
+ * perm entries outside [0, S) or heads outside [0, B*H) set
+ * SAF_DEV_BADINDEX in the device status word and are skipped.
+ * Replaces: process / process_back of SmartAttention (SmartAttention.py:
+ * 16-41), the (t, h, w) <-> (h, w, t) reordering of the video tokens. */
+int32_t saf_permute_tokens(const void* x, void* out, int32_t dtype, int64_t B, int64_t H, int64_t S,
+                           int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss, int64_t o_sb,
+                           int64_t o_sh, int64_t o_ss, const int32_t* perm, const int32_t* heads,
+                           int64_t n_heads, void* stream);
+
+/* Ulysses sequence <-> head layout for the all-to-all of sequence-sharded
+ * attention.  Sequence-sharded tensors are [B, s, H, D] (element strides
+ * stride_b / stride_s / stride_h, D contiguous, D * element size a multiple
+ * of 16 bytes, 16-byte aligned rows); head_off (host array, P + 1 entries,
+ * head_off[0] = 0, head_off[P] = H) gives each peer's contiguous head range.
+ * pack writes T (<= 4) tensors into buf as P chunks back to back, chunk j =
+ * heads of peer j as [s, B, T, h_j, D]; unpack is the inverse.  After an
+ * all-to-all of these chunks a peer holds [S, B, T, h, D]: each tensor a
+ * strided [B, h, S, D] view for saf_bsa_fwd / saf_pool_topk.
+ * Replaces: no reference function (the reference runs on one GPU); these
+ * are the layout steps around the NCCL all-to-all of sequence-sharded runs. */
+int32_t saf_ulysses_pack(void* const* seq, int32_t T, int32_t dtype, int64_t B, int64_t s, int64_t H,
+                         int64_t D, int64_t stride_b, int64_t stride_s, int64_t stride_h,
+                         const int32_t* head_off, int32_t P, void* buf, void* stream);
+int32_t saf_ulysses_unpack(const void* buf, int32_t T, int32_t dtype, int64_t B, int64_t s, int64_t H,
+                           int64_t D, int64_t stride_b, int64_t stride_s, int64_t stride_h,
+                           const int32_t* head_off, int32_t P, void* const* seq, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

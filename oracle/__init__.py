@@ -16,6 +16,8 @@ Modules
                 torch CPU masked SDPA used as the timed CPU baseline.
   tome       -- ToMe bipartite soft matching, merge and unmerge
                 (utils/merge_unmerge.py:34-154).
+  ulysses    -- the pack / unpack layout of the sequence <-> head
+                all-to-all (no reference counterpart: single-GPU reference).
 
 Pinning: ``tests/golden/make_golden.py`` imports the reference from its
 source tree (only where that tree exists, i.e. not on the GPU box) and

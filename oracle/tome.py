@@ -191,3 +191,45 @@ def proportional_bias(counter, text_len: int, unm_len: int) -> np.ndarray:
     bias = np.zeros((B, text_len + unm_len + Nd), dtype=np.float64)
     bias[:, text_len + unm_len:] = np.log(counter.astype(np.float64))
     return bias
+
+
+def round_to_bf16(x: np.ndarray) -> np.ndarray:
+    """fp64 -> nearest bf16 value (ties to even), rounded once from fp64
+    (as __double2bfloat16), returned as fp64."""
+    x = np.asarray(x, dtype=np.float64)
+    m, e = np.frexp(x)                      # x = m * 2**e, 0.5 <= |m| < 1
+    return np.ldexp(np.rint(m * 256.0) / 256.0, e)
+
+
+def kv_metric(k, v, text_len: int):
+    """MergeAttention's metric [k, |k|, v, |v|] of the video tokens
+    (MergeAttention.py:26-31) as [B*H, S - text_len, 2D + 2] in the input's
+    16-bit type.  Each norm follows the saf_tome_kv_metric summation order:
+    lane l of 32 sums (x[2w]^2 + x[2w+1]^2) over its words w = l, l + 32
+    (ascending), the lane sums combine by the xor butterfly 16, 8, 4, 2, 1
+    (all in fp64), then the fp64 sqrt is rounded once to the 16-bit type."""
+    import torch
+
+    B, H, S, D = k.shape
+    parts = []
+    for x in (k, v):
+        xv = x[:, :, text_len:].reshape(B * H, S - text_len, D)
+        f = xv.double().cpu().numpy()
+        sq = f * f
+        pair = sq[..., 0::2] + sq[..., 1::2]            # word w: x[2w]^2 + x[2w+1]^2
+        W = pair.shape[-1]
+        lanes = np.zeros(f.shape[:2] + (32,))
+        for w0 in range(0, W, 32):                       # words l, l + 32, ... ascending
+            chunk = np.zeros(f.shape[:2] + (32,))
+            chunk[..., :min(32, W - w0)] = pair[..., w0:w0 + 32]
+            lanes = lanes + chunk
+        lane = np.arange(32)
+        for m in (16, 8, 4, 2, 1):
+            lanes = lanes + lanes[..., lane ^ m]
+        nrm = np.sqrt(lanes[..., 0])
+        if x.dtype == torch.bfloat16:
+            n16 = torch.from_numpy(round_to_bf16(nrm)).to(torch.bfloat16)
+        else:
+            n16 = torch.from_numpy(nrm.astype(np.float16))
+        parts += [xv.cpu(), n16.unsqueeze(-1)]
+    return torch.cat(parts, dim=-1)

@@ -112,12 +112,21 @@ SIGNATURES = {
     "saf_mask_to_csr": (_I32, [_P, _I64, _I32, _I32, _I64, _I64, _P, _P, _P]),
     "saf_bsa_fwd": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I64, _F32, _I32,
                            _P]),
+    "saf_bsa_fwd_ranges": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I64, _F32,
+                                  _I32, _P, _P]),
     "saf_tome_match_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "saf_tome_match": (_I32, [_P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I32,
                               ctypes.POINTER(TomePlan), _P, _SZ, _P]),
+    "saf_tome_kv_metric": (_I32, [_PT4, _PT4, _I32, _P, _P]),
     "saf_tome_merge": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I64, _P,
                               _I64, _I32, ctypes.POINTER(TomePlan), _P]),
     "saf_tome_unmerge": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I64, _P, _P]),
+    "saf_permute_tokens": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                  _I64, _P, _P, _I64, _P]),
+    "saf_ulysses_pack": (_I32, [_P, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P,
+                                _P]),
+    "saf_ulysses_unpack": (_I32, [_P, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32,
+                                  _P, _P]),
 }
 
 _lib = None

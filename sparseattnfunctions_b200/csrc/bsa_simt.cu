@@ -15,7 +15,8 @@ namespace saf {
 int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
-                      int64_t bias_stride, float sm_scale, int lead_tiles, cudaStream_t stream);
+                      int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
+                      cudaStream_t stream);
 
 namespace {
 
@@ -36,6 +37,7 @@ struct SimtParams {
   int64_t bias_stride;
   float scale;
   unsigned int* status;
+  const int4* row_ranges;  // nullable [Sq]: key intervals [x, y) U [z, w) of each query row
 };
 
 // grid (ceil(Sq/64), B*H), 256 threads.  Thread (ty, tx) in a 16 x 16 grid
@@ -130,8 +132,15 @@ __global__ void __launch_bounds__(256) bsa_fwd_simt_kernel(const SimtParams p) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int kc = tx * 4 + c;
-          ss[(ty * 4 + i) * (kT + 1) + kc] =
-              (k0 + kc < p.Sk) ? s[i][c] * p.scale + bias_s[kc] : -INFINITY;
+          bool keep = k0 + kc < p.Sk;
+          if (p.row_ranges != nullptr) {
+            const int qr = q0 + ty * 4 + i, kk = k0 + kc;
+            if (qr < p.Sq) {
+              const int4 rr = __ldg(p.row_ranges + qr);
+              keep = keep && ((kk >= rr.x && kk < rr.y) || (kk >= rr.z && kk < rr.w));
+            }
+          }
+          ss[(ty * 4 + i) * (kT + 1) + kc] = keep ? s[i][c] * p.scale + bias_s[kc] : -INFINITY;
         }
       __syncthreads();
       // Row softmax update: the 16 threads of row group ty split the columns.
@@ -192,7 +201,8 @@ __global__ void __launch_bounds__(256) bsa_fwd_simt_kernel(const SimtParams p) {
 int32_t bsa_fwd_simt(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
                      const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                      int64_t col_capacity, int bm, int bn, const float* kv_bias,
-                     int64_t bias_stride, float sm_scale, cudaStream_t stream) {
+                     int64_t bias_stride, float sm_scale, const int32_t* row_ranges,
+                     cudaStream_t stream) {
   if (bm % kT != 0 || bn % kT != 0) return SAF_ERR_UNSUPPORTED;
   if (q->D != 64 && q->D != 128) return SAF_ERR_UNSUPPORTED;
   SimtParams p{};
@@ -217,6 +227,7 @@ int32_t bsa_fwd_simt(const saf_tensor4* q, const saf_tensor4* k, const saf_tenso
   p.kv_bias = kv_bias;
   p.bias_stride = bias_stride;
   p.scale = sm_scale;
+  p.row_ranges = reinterpret_cast<const int4*>(row_ranges);
   p.status = device_status_ptr();
   if (p.status == nullptr) return SAF_ERR_CUDA;
   dim3 grid(static_cast<unsigned>((q->S + kT - 1) / kT), static_cast<unsigned>(q->B * q->H));
@@ -248,11 +259,13 @@ int32_t check_operand(const saf_tensor4* t, const saf_tensor4* ref) {
 
 using namespace saf;
 
-extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
-                               const saf_tensor4* o, const int32_t* row_ptr,
-                               const int32_t* col_idx, int64_t col_capacity, int32_t block_m,
-                               int32_t block_n, const float* kv_bias, int64_t kv_bias_stride_bh,
-                               float sm_scale, int32_t lead_rows, void* stream) {
+extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k,
+                                      const saf_tensor4* v, const saf_tensor4* o,
+                                      const int32_t* row_ptr, const int32_t* col_idx,
+                                      int64_t col_capacity, int32_t block_m, int32_t block_n,
+                                      const float* kv_bias, int64_t kv_bias_stride_bh,
+                                      float sm_scale, int32_t lead_rows, const int32_t* row_ranges,
+                                      void* stream) {
   int32_t rc = check_tensor4(q);
   if (rc != SAF_OK) return rc;
   if ((rc = check_operand(k, q)) != SAF_OK) return rc;
@@ -264,11 +277,13 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
   if (kv_bias_stride_bh < 0) return SAF_ERR_STRIDE;
   if (lead_rows < 0) return SAF_ERR_ARG;
   if (q->S > 0x7fffffff || k->S > 0x7fffffff || q->B * q->H > 65535) return SAF_ERR_SHAPE;
+  if (row_ranges != nullptr && (reinterpret_cast<uintptr_t>(row_ranges) & 15) != 0) return SAF_ERR_STRIDE;
+  if (row_ranges != nullptr && kv_bias != nullptr) return SAF_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (q->dtype == SAF_F32) {
     if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
     return bsa_fwd_simt(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
-                        kv_bias_stride_bh, sm_scale, st);
+                        kv_bias_stride_bh, sm_scale, row_ranges, st);
   }
   // 16-bit path: tcgen05 kernel; tiles of 64 or 128, 16-byte aligned rows.
   if ((block_m != 64 && block_m != 128) || (block_n != 64 && block_n != 128))
@@ -285,5 +300,14 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
   const int64_t lead_tiles = (static_cast<int64_t>(lead_rows) * block_m + 127) / 128;
   return bsa_fwd_sm100(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                        kv_bias_stride_bh, sm_scale,
-                       static_cast<int>(lead_tiles < 65535 ? lead_tiles : 65535), st);
+                       static_cast<int>(lead_tiles < 65535 ? lead_tiles : 65535), row_ranges, st);
+}
+
+extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                               const saf_tensor4* o, const int32_t* row_ptr,
+                               const int32_t* col_idx, int64_t col_capacity, int32_t block_m,
+                               int32_t block_n, const float* kv_bias, int64_t kv_bias_stride_bh,
+                               float sm_scale, int32_t lead_rows, void* stream) {
+  return saf_bsa_fwd_ranges(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
+                            kv_bias_stride_bh, sm_scale, lead_rows, nullptr, stream);
 }

@@ -68,6 +68,9 @@ struct BsaParams {
   unsigned int* status;
   uint64_t budget_ns;
   int lead_tiles;  // query tiles per head scheduled first
+  // nullable [Sq] int4: the key columns of query row r are limited to
+  // [x, y) U [z, w) (frame-band masks); shared by every head
+  const int4* row_ranges;
 };
 
 // Iterates the live kv tiles of one 128-row query tile.  With 64-row mask
@@ -196,7 +199,7 @@ struct Layout {
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
 };
 
-template <int BN, bool kBias, bool kBF16>
+template <int BN, bool kBias, bool kBF16, bool kRanges>
 __global__ void __launch_bounds__(kThreads, 2)
     bsa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -426,6 +429,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     const f2 sl2x2 = mk2(sl2, sl2);
 
     float m_run = -INFINITY, l_run = 0.f;
+    // key intervals of this thread's query row (kRanges)
+    int lo0 = 0, hi0 = 0, lo1 = 0, hi1 = 0;
+    if constexpr (kRanges) {
+      if (q0 + row < p.Sq) {
+        const int4 rr = __ldg(p.row_ranges + q0 + row);
+        lo0 = rr.x, hi0 = rr.y, lo1 = rr.z, hi1 = rr.w;
+      }
+    }
     TileIter it;
     it.init(p, g, tile);
     int j = 0, col;
@@ -451,8 +462,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(bar_s_empty);
 
       const bool live = (rm >> rhalf) & 1u;
-      const int valid = p.Sk - col * BN - chalf * HC;  // valid columns of this half
-      const bool fast = live && valid >= HC;             // warp-uniform
+      const int c0 = col * BN + chalf * HC;  // first key column of this half
+      const int valid = p.Sk - c0;           // valid columns of this half
+      bool fast = live && valid >= HC;       // warp-uniform without kRanges
+      if constexpr (kRanges)
+        fast = fast && ((c0 >= lo0 && c0 + HC <= hi0) || (c0 >= lo1 && c0 + HC <= hi1));
       float t[HC];
       if constexpr (kBias) {
         const int sv = j % kVS;
@@ -475,9 +489,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int e = 0; e < HC; ++e) t[e] = __uint_as_float(r(e));
       }
       if (!fast) {
+        if constexpr (kRanges) {
+          const int a0 = lo0 - c0, b0 = hi0 - c0, a1 = lo1 - c0, b1 = hi1 - c0;
 #pragma unroll
-        for (int e = 0; e < HC; ++e)
-          if (!(live && e < valid)) t[e] = -INFINITY;
+          for (int e = 0; e < HC; ++e)
+            if (!(live && e < valid && ((e >= a0 && e < b0) || (e >= a1 && e < b1)))) t[e] = -INFINITY;
+        } else {
+#pragma unroll
+          for (int e = 0; e < HC; ++e)
+            if (!(live && e < valid)) t[e] = -INFINITY;
+        }
       }
       // Under lazy rescaling the running max rarely moves, so P is computed
       // speculatively with the current running max while the block max is
@@ -672,10 +693,10 @@ int32_t make_qkv_map(CUtensorMap* map, const saf_tensor4* t, int rows) {
   return r == CUDA_SUCCESS ? SAF_OK : SAF_ERR_STRIDE;
 }
 
-template <int BN, bool kBias, bool kBF16>
+template <int BN, bool kBias, bool kBF16, bool kRanges>
 int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                        const BsaParams& p, int n_tiles, cudaStream_t stream) {
-  auto kern = bsa_fwd_sm100_kernel<BN, kBias, kBF16>;
+  auto kern = bsa_fwd_sm100_kernel<BN, kBias, kBF16, kRanges>;
   const int smem = Layout<BN>::kDynSmem;
   SAF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid(n_tiles, p.B * p.H);
@@ -690,8 +711,10 @@ int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
 int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
-                      int64_t bias_stride, float sm_scale, int lead_tiles, cudaStream_t stream) {
+                      int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
+                      cudaStream_t stream) {
   if (q->D != kD) return SAF_ERR_UNSUPPORTED;
+  if (row_ranges != nullptr && kv_bias != nullptr) return SAF_ERR_UNSUPPORTED;
   if (!current_device_is_sm100()) return SAF_ERR_UNSUPPORTED;
   CUtensorMap mq, mk, mv;
   int32_t rc;
@@ -719,21 +742,27 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   p.status = device_status_ptr();
   p.budget_ns = wait_budget_ns();
   p.lead_tiles = lead_tiles;
+  p.row_ranges = reinterpret_cast<const int4*>(row_ranges);
   if (p.status == nullptr) return SAF_ERR_CUDA;
   const int n_tiles = static_cast<int>((q->S + kBM - 1) / kBM);
   const bool bf16 = q->dtype == SAF_BF16;
   const bool bias = kv_bias != nullptr;
-#define SAF_BSA_CASE(BN_, BIAS_, BF_)                                 \
-  if (bn == BN_ && bias == BIAS_ && bf16 == BF_)                      \
-    return launch_variant<BN_, BIAS_, BF_>(mq, mk, mv, p, n_tiles, stream);
-  SAF_BSA_CASE(128, false, true)
-  SAF_BSA_CASE(128, true, true)
-  SAF_BSA_CASE(128, false, false)
-  SAF_BSA_CASE(128, true, false)
-  SAF_BSA_CASE(64, false, true)
-  SAF_BSA_CASE(64, true, true)
-  SAF_BSA_CASE(64, false, false)
-  SAF_BSA_CASE(64, true, false)
+  const bool ranges = row_ranges != nullptr;
+#define SAF_BSA_CASE(BN_, BIAS_, BF_, RG_)                                 \
+  if (bn == BN_ && bias == BIAS_ && bf16 == BF_ && ranges == RG_)          \
+    return launch_variant<BN_, BIAS_, BF_, RG_>(mq, mk, mv, p, n_tiles, stream);
+  SAF_BSA_CASE(128, false, true, false)
+  SAF_BSA_CASE(128, true, true, false)
+  SAF_BSA_CASE(128, false, false, false)
+  SAF_BSA_CASE(128, true, false, false)
+  SAF_BSA_CASE(64, false, true, false)
+  SAF_BSA_CASE(64, true, true, false)
+  SAF_BSA_CASE(64, false, false, false)
+  SAF_BSA_CASE(64, true, false, false)
+  SAF_BSA_CASE(128, false, true, true)
+  SAF_BSA_CASE(128, false, false, true)
+  SAF_BSA_CASE(64, false, true, true)
+  SAF_BSA_CASE(64, false, false, true)
 #undef SAF_BSA_CASE
   return SAF_ERR_UNSUPPORTED;
 }

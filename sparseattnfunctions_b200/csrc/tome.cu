@@ -47,7 +47,8 @@ constexpr double kEps = 1.0 / 4096.0;  // accumulation error bound / (|a| |b|)
 
 struct ScoreParams {
   int B, Ns, Nd, Cp;
-  const float* rinv_b;  // [B, Nd] 1 / |b| (fp32)
+  const double* na;     // [B, Ns] squared norms of the src rows (fp64)
+  const float* rinv_b;  // [B, Nd rounded up to 4] 1 / |b| (fp32; rows 16-byte aligned)
   int32_t* cand_idx;    // [B, Ns, 8]
   float* cand_val;      // [B, Ns, 8]
   unsigned int* status;
@@ -197,7 +198,16 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const int quarter = warp & 3, chalf = (warp - 4) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const float* rinv = p.rinv_b + static_cast<int64_t>(b) * p.Nd;
+    const float* rinv = p.rinv_b + static_cast<int64_t>(b) * ((p.Nd + 3) & ~3);
+    // Candidates of this thread's half of the row: every column whose score
+    // came within tau of the running maximum when it was seen (the only
+    // columns that can hold the exact best, as each score is within tau / 2
+    // of its exact value), at most kCand of them, in descending order.  A
+    // column still within tau that does not fit sets `ovf`: the row then
+    // takes the exact full scan.  tau is widened by 1/256 so that fp32
+    // rounding of the comparisons cannot drop a candidate.
+    const double na_row = m0 + row < p.Ns ? p.na[static_cast<int64_t>(b) * p.Ns + m0 + row] : 0.0;
+    const float tau = static_cast<float>(2.0 * kEps * sqrt(na_row) * (1.0 + 1.0 / 256.0));
     float cv[kCand];
     int ci[kCand];
 #pragma unroll
@@ -205,6 +215,12 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       cv[i] = -INFINITY;
       ci[i] = -1;
     }
+    float run_max = -INFINITY;
+    bool ovf = false;
+    auto add = [&](float sv, int j, float thr) {
+      if (ci[kCand - 1] >= 0 && fminf(sv, cv[kCand - 1]) >= thr) ovf = true;
+      cand_insert(cv, ci, sv, j);
+    };
     bool ok = true;
     for (int nt = 0; nt < n_tiles; ++nt) {
       const int buf = nt & 1;
@@ -225,27 +241,74 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           mbar_arrive(bar_acc_empty(buf));
         }
         const int jc = col0 + c * 32;
+        // scores of the chunk (1/|b| from vector loads every lane of the warp
+        // shares); columns past Nd score -inf
+        float sc[32];
+        if (jc + 32 <= p.Nd) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = jc + e;
-          if (j < p.Nd) cand_insert(cv, ci, __uint_as_float(r[e]) * __ldg(rinv + j), j);
+          for (int e = 0; e < 32; e += 4) {
+            const float4 rv = __ldg(reinterpret_cast<const float4*>(rinv + jc + e));
+            const f2 a = mul2(mk2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), mk2(rv.x, rv.y));
+            const f2 b2 = mul2(mk2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])), mk2(rv.z, rv.w));
+            sc[e] = lo2(a);
+            sc[e + 1] = hi2(a);
+            sc[e + 2] = lo2(b2);
+            sc[e + 3] = hi2(b2);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            sc[e] = jc + e < p.Nd ? __uint_as_float(r[e]) * __ldg(rinv + jc + e) : -INFINITY;
+        }
+        float mx = fmax3(sc[0], sc[1], sc[2]);
+#pragma unroll
+        for (int e = 3; e < 31; e += 2) mx = fmax3(mx, sc[e], sc[e + 1]);
+        mx = fmaxf(mx, sc[31]);
+        // most chunks hold nothing within tau of the running maximum
+        if (mx >= run_max - tau) {
+          run_max = fmaxf(run_max, mx);
+          const float thr = run_max - tau;
+          int cnt = 0, first = 0;
+#pragma unroll
+          for (int e = 31; e >= 0; --e) {
+            if (sc[e] >= thr) {
+              ++cnt;
+              first = e;
+            }
+          }
+          if (cnt == 1) {
+            add(mx, jc + first, thr);  // the chunk maximum, usually alone
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (sc[e] >= thr) add(sc[e], jc + e, thr);
+          }
         }
       }
     }
     // merge the two column halves of every row
     float2* cand = reinterpret_cast<float2*>(smem + L::kOffCand);
+    if (chalf == 1) {
 #pragma unroll
-    for (int i = 0; i < kCand; ++i)
-      cand[(chalf * kTM + row) * kCand + i] = make_float2(cv[i], __int_as_float(ci[i]));
+      for (int i = 0; i < kCand; ++i)
+        cand[(kTM + row) * kCand + i] = make_float2(cv[i], __int_as_float(ci[i]));
+      cand[row * kCand] = make_float2(run_max, __int_as_float(ovf ? 1 : 0));
+    }
     mbar_arrive(bar_xend);
     const bool have = ok && __all_sync(0xffffffffu, mbar_wait(bar_xend, 0, abort_flag, p.status,
                                                                p.budget_ns));
     if (have && chalf == 0 && m0 + row < p.Ns && !*abort_flag) {
+      const float2 hdr = cand[row * kCand];
+      run_max = fmaxf(run_max, hdr.x);
+      ovf = ovf || __float_as_int(hdr.y) != 0;
+      const float thr = run_max - tau;
 #pragma unroll
       for (int i = 0; i < kCand; ++i) {
         const float2 o = cand[(kTM + row) * kCand + i];
-        cand_insert(cv, ci, o.x, __float_as_int(o.y));
+        if (__float_as_int(o.y) >= 0 && o.x >= thr) add(o.x, __float_as_int(o.y), thr);
       }
+      // an incomplete row is marked by candidate index -2 in the last slot
+      if (ovf) ci[kCand - 1] = -2;
       const int64_t base = (static_cast<int64_t>(b) * p.Ns + m0 + row) * kCand;
 #pragma unroll
       for (int i = 0; i < kCand; ++i) {
@@ -283,7 +346,7 @@ struct GatherParams {
   int n_rows;
   void* out;           // [B, n_rows, Cp] 16-bit
   double* sqnorm;      // [B, n_rows]
-  float* rinv;         // [B, n_rows] or null
+  float* rinv;         // [B, n_rows rounded up to 4] or null
   unsigned int* status;
 };
 
@@ -312,7 +375,7 @@ __global__ void __launch_bounds__(256) tome_gather_kernel(const GatherParams g) 
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (lane == 0) {
     g.sqnorm[static_cast<int64_t>(b) * g.n_rows + warp] = acc;
-    if (g.rinv) g.rinv[static_cast<int64_t>(b) * g.n_rows + warp] = static_cast<float>(1.0 / sqrt(acc));
+    if (g.rinv) g.rinv[static_cast<int64_t>(b) * ((g.n_rows + 3) & ~3) + warp] = static_cast<float>(1.0 / sqrt(acc));
   }
 }
 
@@ -350,9 +413,12 @@ __global__ void __launch_bounds__(256) tome_exact_kernel(const ExactParams e) {
   const float* cv = e.cand_val + ri * kCand;
   const int32_t* ci = e.cand_idx + ri * kCand;
   const double tau = 2.0 * kEps * sa;  // in units of s~ = dot * (1/|b|)
-  const bool complete = e.Nd <= kCand ||
-                        (static_cast<double>(cv[0]) - static_cast<double>(cv[kCand - 1]) > tau &&
-                         ci[kCand - 1] >= 0);
+  // The score kernel kept every column within tau of the row's maximum
+  // unless it marked the row incomplete (index -2 in the last slot).
+  const bool complete = e.Nd <= kCand || ci[kCand - 1] != -2;
+  // A candidate can be the exact best only if its tensor-core score is within
+  // tau of the top one (each score is within tau / 2 of its exact value).
+  const float keep_above = static_cast<float>(static_cast<double>(cv[0]) - tau * (1.0 + 1.0 / 256.0));
   double best = -INFINITY;
   int bj = 0x7fffffff;
   auto consider = [&](int j) {
@@ -368,7 +434,7 @@ __global__ void __launch_bounds__(256) tome_exact_kernel(const ExactParams e) {
 #pragma unroll 1
     for (int k = 0; k < kCand && k < e.Nd; ++k) {
       const int j = ci[k];
-      if (j >= 0) consider(j);
+      if (j >= 0 && (k == 0 || cv[k] >= keep_above)) consider(j);
     }
   } else {
 #pragma unroll 1
@@ -532,6 +598,80 @@ __global__ void __launch_bounds__(256) tome_unmerge_kernel(const RowCopyParams q
   }
 }
 
+// Vectorised forms: one thread per 16-byte chunk of an output row, so rows
+// narrower than a warp's 512 bytes (the per-head D = 64 layout of merged
+// attention) still keep every lane busy.  Used when every row start is
+// 16-byte aligned; the warp-per-row kernels above cover the rest.
+template <typename T>
+struct Vec16 {
+  static constexpr int kN = 16 / static_cast<int>(sizeof(T));
+};
+
+template <typename T>
+__device__ __forceinline__ void acc16(float (&a)[Vec16<T>::kN], const uint4 v) {
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < Vec16<T>::kN; ++i) a[i] += to_f(e[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) tome_merge_vec_kernel(const RowCopyParams q, const int chunks,
+                                                             const int64_t total) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int row = static_cast<int>(idx / chunks), ch = static_cast<int>(idx - static_cast<int64_t>(row) * chunks);
+  const int b = blockIdx.y;
+  const int64_t bo = b;
+  const int unm_len = q.Ns - q.r;
+  const T* xb = static_cast<const T*>(q.x) + bo * q.x_sb;
+  uint4* op = reinterpret_cast<uint4*>(static_cast<T*>(q.out) + bo * q.o_sb + static_cast<int64_t>(row) * q.o_sn) + ch;
+  if (row < q.text + unm_len) {
+    const int src_row = row < q.text ? row : q.text + q.a_idx[q.unm_idx[bo * unm_len + row - q.text]];
+    *op = __ldg(reinterpret_cast<const uint4*>(xb + static_cast<int64_t>(src_row) * q.x_sn) + ch);
+    return;
+  }
+  // dst row: (x_dst + merged src rows in ascending merge order) / counter, in fp32
+  constexpr int kN = Vec16<T>::kN;
+  const int j = row - q.text - unm_len;
+  float a[kN];
+#pragma unroll
+  for (int i = 0; i < kN; ++i) a[i] = 0.f;
+  acc16<T>(a, __ldg(reinterpret_cast<const uint4*>(xb + static_cast<int64_t>(q.text + q.b_idx[j]) * q.x_sn) + ch));
+  const int p0 = q.dst_ptr[bo * (q.Nd + 1) + j], p1 = q.dst_ptr[bo * (q.Nd + 1) + j + 1];
+  for (int t = p0; t < p1; ++t) {
+    const int s = q.dst_src[bo * q.r + t];
+    acc16<T>(a, __ldg(reinterpret_cast<const uint4*>(xb + static_cast<int64_t>(q.text + q.a_idx[s]) * q.x_sn) + ch));
+  }
+  const float inv = 1.f / static_cast<float>(q.counter[bo * q.Nd + j]);
+  uint4 o;
+  T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+  for (int i = 0; i < kN; ++i) oe[i] = from_f<T>(a[i] * inv);
+  *op = o;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) tome_unmerge_vec_kernel(const RowCopyParams q, const int chunks,
+                                                               const int64_t total) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int row = static_cast<int>(idx / chunks), ch = static_cast<int>(idx - static_cast<int64_t>(row) * chunks);
+  const int64_t bo = blockIdx.y;
+  const int src_row = row < q.text ? row : q.text + q.token_map[bo * q.N + row - q.text];
+  const uint4* xs = reinterpret_cast<const uint4*>(static_cast<const T*>(q.x) + bo * q.x_sb +
+                                                   static_cast<int64_t>(src_row) * q.x_sn) + ch;
+  uint4* op = reinterpret_cast<uint4*>(static_cast<T*>(q.out) + bo * q.o_sb + static_cast<int64_t>(row) * q.o_sn) + ch;
+  *op = __ldg(xs);
+}
+
+// True when every row of x and out starts on a 16-byte boundary and C fills whole 16-byte chunks.
+bool rows_vec16(const RowCopyParams& q, size_t elem) {
+  const int64_t v = 16 / static_cast<int64_t>(elem);
+  return (q.C * elem) % 16 == 0 && (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(q.out) & 15) == 0 && q.x_sb % v == 0 && q.x_sn % v == 0 &&
+         q.o_sb % v == 0 && q.o_sn % v == 0;
+}
+
 // ---------------------------------------------------------------------------
 // workspace layout of saf_tome_match
 struct MatchLayout {
@@ -554,7 +694,7 @@ MatchLayout match_layout(int64_t B, int64_t Ns, int64_t Nd, int64_t Cp, int64_t 
   l.off_b = take(B * Nd * Cp * 2);
   l.off_na = take(B * Ns * 8);
   l.off_nb = take(B * Nd * 8);
-  l.off_rinv = take(B * Nd * 4);
+  l.off_rinv = take(B * ((Nd + 3) & ~3) * 4);
   l.off_ci = take(B * Ns * kCand * 4);
   l.off_cv = take(B * Ns * kCand * 4);
   l.off_nmax = take(B * Ns * 8);
@@ -674,7 +814,7 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   if ((rc = make_rows_map(&ma, A, B, Ns, Cp, kTM, bf16)) != SAF_OK) return rc;
   if ((rc = make_rows_map(&mb, Bm, B, Nd, Cp, kTN, bf16)) != SAF_OK) return rc;
   ScoreParams sp{static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd), static_cast<int>(Cp),
-                 rinv, ci, cv, status, wait_budget_ns()};
+                 na, rinv, ci, cv, status, wait_budget_ns()};
   dim3 sg(static_cast<unsigned>((Ns + kTM - 1) / kTM), static_cast<unsigned>(B));
   const int smem = ScoreLayout::kDynSmem;
   if (bf16) {
@@ -738,6 +878,112 @@ int32_t check_rows(const void* p, int32_t dtype) {
 }
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// MergeAttention's matching metric [k, |k|, v, |v|] of the video tokens.
+// One warp per token row: lane l holds the 16-bit pairs at words l, l + 32
+// of the row (coalesced 4-byte loads), squares them in fp64 and adds
+// (x[2w]^2 + x[2w+1]^2) for its words in ascending order; the lanes' sums are
+// combined by the xor butterfly 16, 8, 4, 2, 1; the fp64 sqrt is rounded
+// once to the 16-bit type.
+namespace saf {
+namespace {
+constexpr int kKvMaxD = 128;
+constexpr int kKvRowsPerWarp = 4;
+
+struct KvMetricParams {
+  const void* k;
+  const void* v;
+  void* out;  // [B*H, S - text, 2D + 2]
+  int64_t k_sb, k_sh, k_ss, v_sb, v_sh, v_ss;
+  int H, S, D, text;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) tome_kv_metric_kernel(const KvMetricParams p) {
+  const int N = p.S - p.text;
+  const int g = blockIdx.y, b = g / p.H, h = g % p.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = p.D / 2, C = 2 * p.D + 2;
+  const int n_first = (blockIdx.x * 8 + warp) * kKvRowsPerWarp;
+  const T* kb = static_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
+  const T* vb = static_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+  uint32_t w[kKvRowsPerWarp][2][2];
+#pragma unroll
+  for (int r = 0; r < kKvRowsPerWarp; ++r) {
+    const int n = n_first + r;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      const T* x = (part == 0 ? kb : vb) + static_cast<int64_t>(p.text + n) * (part == 0 ? p.k_ss : p.v_ss);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int word = lane + 32 * i;
+        w[r][part][i] = (n < N && word < W) ? __ldg(reinterpret_cast<const uint32_t*>(x) + word) : 0u;
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kKvRowsPerWarp; ++r) {
+    const int n = n_first + r;
+    if (n >= N) break;
+    T* o = static_cast<T*>(p.out) + (static_cast<int64_t>(g) * N + n) * C;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      double acc = 0.0;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int word = lane + 32 * i;
+        if (word < W) {
+          const T* e = reinterpret_cast<const T*>(&w[r][part][i]);
+          const double a = static_cast<double>(to_f(e[0])), c = static_cast<double>(to_f(e[1]));
+          acc = __dadd_rn(acc, __dadd_rn(__dmul_rn(a, a), __dmul_rn(c, c)));
+          T* od = o + part * (p.D + 1) + 2 * word;
+          od[0] = e[0];
+          od[1] = e[1];
+        }
+      }
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+      if (lane == 0) {
+        const double nrm = sqrt(acc);
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) o[part * (p.D + 1) + p.D] = __double2bfloat16(nrm);
+        else o[part * (p.D + 1) + p.D] = __double2half(nrm);
+      }
+    }
+  }
+}
+}  // namespace
+}  // namespace saf
+
+extern "C" int32_t saf_tome_kv_metric(const saf_tensor4* k, const saf_tensor4* v, int32_t text_len,
+                                      void* out, void* stream) {
+  if (k == nullptr || v == nullptr || out == nullptr) return SAF_ERR_ARG;
+  int32_t rc;
+  if ((rc = check_tensor4(k)) != SAF_OK || (rc = check_tensor4(v)) != SAF_OK) return rc;
+  if (k->dtype != v->dtype) return SAF_ERR_DTYPE;
+  if (k->dtype != SAF_BF16 && k->dtype != SAF_F16) return SAF_ERR_DTYPE;
+  if (k->B != v->B || k->H != v->H || k->S != v->S || k->D != v->D) return SAF_ERR_SHAPE;
+  if (text_len < 0 || text_len >= k->S || k->B * k->H > 65535) return SAF_ERR_SHAPE;
+  if (k->D % 2 != 0 || k->D > kKvMaxD) return SAF_ERR_UNSUPPORTED;
+  const saf_tensor4* kv[2] = {k, v};
+  for (const saf_tensor4* x : kv)  // 4-byte aligned rows for the staged loads
+    if ((reinterpret_cast<uintptr_t>(x->data) & 3) != 0 || x->stride_s % 2 || x->stride_h % 2 ||
+        x->stride_b % 2)
+      return SAF_ERR_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(out) & 3) != 0) return SAF_ERR_STRIDE;
+  if ((rc = bind_device_of(k->data)) != SAF_OK) return rc;
+  KvMetricParams p{k->data, v->data, out, k->stride_b, k->stride_h, k->stride_s, v->stride_b,
+                   v->stride_h, v->stride_s, static_cast<int>(k->H), static_cast<int>(k->S),
+                   static_cast<int>(k->D), text_len};
+  const int N = static_cast<int>(k->S) - text_len;
+  const int per_cta = 8 * kKvRowsPerWarp;
+  dim3 grid(static_cast<unsigned>((N + per_cta - 1) / per_cta), static_cast<unsigned>(k->B * k->H));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k->dtype == SAF_BF16) tome_kv_metric_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+  else tome_kv_metric_kernel<__half><<<grid, 256, 0, st>>>(p);
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}
+
 extern "C" int32_t saf_tome_merge(const void* x, void* out, int32_t dtype, int64_t B, int64_t C,
                                   int64_t x_stride_b, int64_t x_stride_n, int64_t o_stride_b,
                                   int64_t o_stride_n, int32_t text_len, const int32_t* a_idx,
@@ -757,8 +1003,21 @@ extern "C" int32_t saf_tome_merge(const void* x, void* out, int32_t dtype, int64
                   static_cast<int>(C), text_len, static_cast<int>(Ns), static_cast<int>(Nd), r, 0,
                   a_idx, b_idx, plan->unm_idx, plan->counter, plan->dst_ptr, plan->dst_src, nullptr};
   const int64_t rows = text_len + (Ns - r) + Nd;
-  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(B));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t elem = dtype == SAF_F32 ? 4 : 2;
+  if (rows_vec16(q, elem)) {
+    const int chunks = static_cast<int>(C * static_cast<int64_t>(elem) / 16);
+    const int64_t total = rows * chunks;
+    dim3 vgrid(static_cast<unsigned>((total + 255) / 256), static_cast<unsigned>(B));
+    switch (dtype) {
+      case SAF_BF16: tome_merge_vec_kernel<__nv_bfloat16><<<vgrid, 256, 0, st>>>(q, chunks, total); break;
+      case SAF_F16: tome_merge_vec_kernel<__half><<<vgrid, 256, 0, st>>>(q, chunks, total); break;
+      default: tome_merge_vec_kernel<float><<<vgrid, 256, 0, st>>>(q, chunks, total); break;
+    }
+    SAF_CUDA_TRY(cudaGetLastError());
+    return SAF_OK;
+  }
+  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(B));
   switch (dtype) {
     case SAF_BF16: tome_merge_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(q); break;
     case SAF_F16: tome_merge_kernel<__half><<<grid, 256, 0, st>>>(q); break;
@@ -782,8 +1041,21 @@ extern "C" int32_t saf_tome_unmerge(const void* y, void* out, int32_t dtype, int
                   static_cast<int>(C), text_len, 0, 0, 0, static_cast<int>(N), nullptr, nullptr,
                   nullptr, nullptr, nullptr, nullptr, token_map};
   const int64_t rows = text_len + N;
-  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(B));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t elem = dtype == SAF_F32 ? 4 : 2;
+  if (rows_vec16(q, elem)) {
+    const int chunks = static_cast<int>(C * static_cast<int64_t>(elem) / 16);
+    const int64_t total = rows * chunks;
+    dim3 vgrid(static_cast<unsigned>((total + 255) / 256), static_cast<unsigned>(B));
+    switch (dtype) {
+      case SAF_BF16: tome_unmerge_vec_kernel<__nv_bfloat16><<<vgrid, 256, 0, st>>>(q, chunks, total); break;
+      case SAF_F16: tome_unmerge_vec_kernel<__half><<<vgrid, 256, 0, st>>>(q, chunks, total); break;
+      default: tome_unmerge_vec_kernel<float><<<vgrid, 256, 0, st>>>(q, chunks, total); break;
+    }
+    SAF_CUDA_TRY(cudaGetLastError());
+    return SAF_OK;
+  }
+  dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(B));
   switch (dtype) {
     case SAF_BF16: tome_unmerge_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(q); break;
     case SAF_F16: tome_unmerge_kernel<__half><<<grid, 256, 0, st>>>(q); break;

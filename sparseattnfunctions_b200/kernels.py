@@ -171,11 +171,15 @@ def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int, dense_rows
 
 
 def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm_scale: float,
-            kv_bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+            kv_bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+            row_ranges: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Block-sparse attention over the live blocks of ``csr``.
 
     ``kv_bias``: optional fp32 additive bias per key column, shape ``[Sk]``
     (shared by all heads), ``[B*H, Sk]`` or ``[B, H, Sk]`` / ``[B, H, 1, Sk]``.
+    ``row_ranges``: optional int32 ``[Sq, 4]`` -- query row r sees only the
+    keys in ``[x, y) U [z, w)`` (frame-band masks; shared by all heads; not
+    combinable with ``kv_bias``).
     """
     dev = _require_cuda(q, k, v)
     q, k, v = _d_last(q), _d_last(k), _d_last(v)
@@ -200,14 +204,54 @@ def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm
         kv_bias = kb  # keep alive for the launch
         bias_ptr = kb.data_ptr()
         bias_stride = 0 if kb.shape[0] == 1 else Sk
+    rr_ptr = None
+    if row_ranges is not None:
+        _require_cuda(row_ranges)
+        if row_ranges.dtype != torch.int32 or tuple(row_ranges.shape) != (Sq, 4) or \
+                not row_ranges.is_contiguous():
+            raise ValueError(f"row_ranges must be a contiguous int32 [{Sq}, 4] tensor")
+        rr_ptr = row_ranges.data_ptr()
     tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
     with torch.cuda.device(dev):
-        rc = _lib.load().saf_bsa_fwd(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
-                                     ctypes.byref(to), csr.row_ptr.data_ptr(), csr.col_idx.data_ptr(),
-                                     csr.col_idx.numel(), csr.block_m, csr.block_n, bias_ptr,
-                                     bias_stride, float(sm_scale), int(csr.dense_rows),
-                                     _stream_ptr(dev))
+        rc = _lib.load().saf_bsa_fwd_ranges(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                                            ctypes.byref(to), csr.row_ptr.data_ptr(),
+                                            csr.col_idx.data_ptr(), csr.col_idx.numel(), csr.block_m,
+                                            csr.block_n, bias_ptr, bias_stride, float(sm_scale),
+                                            int(csr.dense_rows), rr_ptr, _stream_ptr(dev))
     _lib.check("saf_bsa_fwd", rc)
+    return out
+
+
+def permute_tokens(x: torch.Tensor, perm: torch.Tensor, heads: Optional[torch.Tensor] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out[b, h, s] = x[b, h, perm[s]]`` for ``[B, H, S, D]`` tensors, for
+    the flat heads ``b*H + h`` in ``heads`` (int32; all heads when None;
+    other heads of ``out`` are left untouched)."""
+    dev = _require_cuda(x, perm)
+    x = _d_last(x)
+    if x.dim() != 4 or x.dtype not in _DTYPES:
+        raise ValueError("expected a [B, H, S, D] bf16 / f16 / f32 tensor")
+    B, H, S, D = x.shape
+    if perm.dtype != torch.int32 or perm.numel() != S or not perm.is_contiguous():
+        raise ValueError(f"perm must be a contiguous int32 tensor of {S} entries")
+    if out is None:
+        out = torch.empty_like(x)
+    if out.shape != x.shape or out.dtype != x.dtype or out.stride(-1) != 1:
+        raise ValueError("out must match x in shape and dtype, D contiguous")
+    hp, nh = None, 0
+    if heads is not None:
+        _require_cuda(heads)
+        if heads.dtype != torch.int32 or not heads.is_contiguous():
+            raise ValueError("heads must be a contiguous int32 tensor")
+        hp, nh = heads.data_ptr(), heads.numel()
+        if nh == 0:
+            return out
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_permute_tokens(x.data_ptr(), out.data_ptr(), _DTYPES[x.dtype], B, H, S, D,
+                                            x.stride(0), x.stride(1), x.stride(2), out.stride(0),
+                                            out.stride(1), out.stride(2), perm.data_ptr(), hp, nh,
+                                            _stream_ptr(dev))
+    _lib.check("saf_permute_tokens", rc)
     return out
 
 
@@ -295,6 +339,24 @@ def tome_match(metric: torch.Tensor, a_idx: torch.Tensor, b_idx: torch.Tensor, r
     return plan
 
 
+def tome_kv_metric(k: torch.Tensor, v: torch.Tensor, text_len: int) -> torch.Tensor:
+    """MergeAttention's matching metric ``[k, |k|, v, |v|]`` of the video
+    tokens (rows ``text_len..`` of ``[B, H, S, D]`` k / v) as
+    ``[B*H, S - text_len, 2D + 2]``; norms from fp64 sums of squares."""
+    dev = _require_cuda(k, v)
+    k, v = _d_last(k), _d_last(v)
+    if k.dtype not in _T16 or v.dtype != k.dtype:
+        raise ValueError("k and v must be bf16 or f16 of the same dtype")
+    B, H, S, D = k.shape
+    out = torch.empty(B * H, S - text_len, 2 * D + 2, dtype=k.dtype, device=dev)
+    tk, tv = _t4(k), _t4(v)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_tome_kv_metric(ctypes.byref(tk), ctypes.byref(tv), int(text_len), out.data_ptr(),
+                                            _stream_ptr(dev))
+    _lib.check("saf_tome_kv_metric", rc)
+    return out
+
+
 def _rows3(x: torch.Tensor, B: int) -> torch.Tensor:
     """[B, rows, C] view of x; a 4-D [b, h, S, D] tensor with b*h == B is
     read as [b*h, S, D] (the per-head matching of MergeAttention)."""
@@ -305,13 +367,23 @@ def _rows3(x: torch.Tensor, B: int) -> torch.Tensor:
     return x if x.stride(-1) == 1 else x.contiguous()
 
 
-def tome_merge(x: torch.Tensor, plan: TomePlan, text_len: int = 0) -> torch.Tensor:
+def _rows_out(out, B, rows, like):
+    if out is None:
+        return torch.empty(B, rows, like.shape[-1], dtype=like.dtype, device=like.device)
+    if tuple(out.shape) != (B, rows, like.shape[-1]) or out.dtype != like.dtype or out.stride(-1) != 1 \
+            or out.device != like.device:
+        raise ValueError(f"out must be a [{B}, {rows}, {like.shape[-1]}] {like.dtype} tensor on {like.device}")
+    return out
+
+
+def tome_merge(x: torch.Tensor, plan: TomePlan, text_len: int = 0,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``x [B, text_len + N, C]`` -> ``[B, text_len + Ns - r + Nd, C]``."""
     dev = _require_cuda(x)
     x = _rows3(x, plan.B)
     if x.shape[1] != text_len + plan.N:
         raise ValueError(f"x has {x.shape[1]} rows, expected text_len + N = {text_len + plan.N}")
-    out = torch.empty(plan.B, text_len + plan.merged_len, x.shape[-1], dtype=x.dtype, device=dev)
+    out = _rows_out(out, plan.B, text_len + plan.merged_len, x)
     st = plan._struct()
     with torch.cuda.device(dev):
         rc = _lib.load().saf_tome_merge(x.data_ptr(), out.data_ptr(), _DTYPES[x.dtype], plan.B,
@@ -323,13 +395,14 @@ def tome_merge(x: torch.Tensor, plan: TomePlan, text_len: int = 0) -> torch.Tens
     return out
 
 
-def tome_unmerge(y: torch.Tensor, plan: TomePlan, text_len: int = 0) -> torch.Tensor:
+def tome_unmerge(y: torch.Tensor, plan: TomePlan, text_len: int = 0,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``y [B, text_len + Ns - r + Nd, C]`` -> ``[B, text_len + N, C]``."""
     dev = _require_cuda(y)
     y = _rows3(y, plan.B)
     if y.shape[1] != text_len + plan.merged_len:
         raise ValueError(f"y has {y.shape[1]} rows, expected {text_len + plan.merged_len}")
-    out = torch.empty(plan.B, text_len + plan.N, y.shape[-1], dtype=y.dtype, device=dev)
+    out = _rows_out(out, plan.B, text_len + plan.N, y)
     with torch.cuda.device(dev):
         rc = _lib.load().saf_tome_unmerge(y.data_ptr(), out.data_ptr(), _DTYPES[y.dtype], plan.B,
                                           y.shape[-1], y.stride(0), y.stride(1), out.stride(0),
@@ -337,3 +410,69 @@ def tome_unmerge(y: torch.Tensor, plan: TomePlan, text_len: int = 0) -> torch.Te
                                           plan.token_map.data_ptr(), _stream_ptr(dev))
     _lib.check("saf_tome_unmerge", rc)
     return out
+
+
+# --------------------------------------------------------------------------- Ulysses layout
+
+def head_split(H: int, P: int) -> list:
+    """Contiguous head ranges of P peers, the first ``H % P`` one head larger
+    (30 heads: 15,15 / 8,8,7,7 / 4,4,4,4,4,4,3,3).  Returns the P + 1 offsets."""
+    if P < 1:
+        raise ValueError("P must be >= 1")
+    base, extra = divmod(H, P)
+    off = [0]
+    for j in range(P):
+        off.append(off[-1] + base + (1 if j < extra else 0))
+    return off
+
+
+def _seq_args(tensors):
+    x = tensors[0]
+    if x.dim() != 4:
+        raise ValueError("expected [B, s, H, D] tensors")
+    for t in tensors[1:]:
+        if t.shape != x.shape or t.stride() != x.stride() or t.dtype != x.dtype:
+            raise ValueError("pack / unpack tensors must share shape, strides and dtype")
+    if x.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {x.dtype}")
+    if x.stride(-1) != 1:
+        raise ValueError("the last (D) dimension must be contiguous")
+    return x
+
+
+def ulysses_pack(tensors, head_off, buf: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Packs T sequence-sharded ``[B, s, H, D]`` tensors into the all-to-all
+    send buffer (P chunks, chunk j = ``[s, B, T, h_j, D]``); returns it flat."""
+    dev = _require_cuda(*tensors)
+    x = _seq_args(tensors)
+    B, s, H, D = x.shape
+    T, P = len(tensors), len(head_off) - 1
+    n = B * s * T * H * D
+    if buf is None:
+        buf = torch.empty(n, dtype=x.dtype, device=dev)
+    elif buf.numel() < n or buf.dtype != x.dtype or not buf.is_contiguous():
+        raise ValueError("send buffer too small, of another dtype or not contiguous")
+    ptrs = (ctypes.c_void_p * T)(*[t.data_ptr() for t in tensors])
+    offs = (ctypes.c_int32 * (P + 1))(*head_off)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_ulysses_pack(ptrs, T, _DTYPES[x.dtype], B, s, H, D, x.stride(0), x.stride(1),
+                                          x.stride(2), offs, P, buf.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_ulysses_pack", rc)
+    return buf
+
+
+def ulysses_unpack(buf: torch.Tensor, outs, head_off) -> None:
+    """Inverse of ``ulysses_pack``: scatters the P received chunks of ``buf``
+    into the T sequence-sharded ``[B, s, H, D]`` tensors ``outs`` (in place)."""
+    dev = _require_cuda(buf, *outs)
+    x = _seq_args(outs)
+    B, s, H, D = x.shape
+    T, P = len(outs), len(head_off) - 1
+    if buf.numel() < B * s * T * H * D or buf.dtype != x.dtype or not buf.is_contiguous():
+        raise ValueError("receive buffer too small, of another dtype or not contiguous")
+    ptrs = (ctypes.c_void_p * T)(*[t.data_ptr() for t in outs])
+    offs = (ctypes.c_int32 * (P + 1))(*head_off)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_ulysses_unpack(buf.data_ptr(), T, _DTYPES[x.dtype], B, s, H, D, x.stride(0),
+                                            x.stride(1), x.stride(2), offs, P, ptrs, _stream_ptr(dev))
+    _lib.check("saf_ulysses_unpack", rc)

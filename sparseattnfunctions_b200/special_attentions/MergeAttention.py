@@ -54,10 +54,7 @@ class MergeAttention:
         text = S - n
         if self.generator is None:
             self.generator = init_generator(k.device)
-        kv = k[:, :, text:].reshape(B * H, n, D)
-        vv = v[:, :, text:].reshape(B * H, n, D)
-        metric = torch.cat((kv, torch.norm(kv, dim=-1, keepdim=True), vv,
-                            torch.norm(vv, dim=-1, keepdim=True)), dim=-1)
+        metric = kernels.tome_kv_metric(k, v, text)  # [k, |k|, v, |v|] per video token
         self.merge_fn, self.unmerge_fn = bipartite_soft_matching_video(
             metric, **cfg, generator=self.generator)
         plan = self.merge_fn.plan

@@ -43,11 +43,13 @@ class BlockSparseAttention:
         return kernels.pool_topk(q, k, block_m=bs, block_n=bs, topk=topk, text_blocks_q=text,
                                  text_blocks_k=text)
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """``out``: optional (possibly strided) ``[B, H, S, D]`` destination."""
         scale = self.sm_scale if self.sm_scale is not None else 1.0 / math.sqrt(q.shape[-1])
         csr = self.select(q, k)
         self.last_csr = csr
-        return kernels.bsa_fwd(q, k, v, csr, scale)
+        return kernels.bsa_fwd(q, k, v, csr, scale, out=out)
 
-    def __call__(self, q, k, v):
-        return self.forward(q, k, v)
+    def __call__(self, q, k, v, out=None):
+        return self.forward(q, k, v, out=out)

@@ -17,6 +17,10 @@ Fixtures
   energy_masks.npz  transfer_attn_to_mask(mode="energy") (SparseGen_Plus.py:12-84)
   tome_*.npz        bipartite_soft_matching_video + merge / unmerge
                     (utils/merge_unmerge.py:34-154), fp64 metric
+  smart_layout.npz  SmartAttention's frame-band mask_mod on a small geometry,
+                    its per-frame key sets at CogVideoX-2B size, and the
+                    process / process_back token orders (SmartAttention.py:
+                    9-43, 90-95)
 """
 from __future__ import annotations
 
@@ -44,6 +48,30 @@ def import_reference(root: str):
     from special_attentions.utils import block_sparse_attn_kernel, merge_unmerge
 
     return block_sparse_attn_kernel, SparseGen_Plus, merge_unmerge
+
+
+def smart_layout(root: str):
+    """Evaluates the reference's SmartAttention layout functions on the CPU."""
+    import torch
+
+    sys.path.insert(0, root)
+    from special_attentions import SmartAttention as sa
+
+    out = {}
+    T, F, n, S = 26, 150, 5, 26 + 5 * 150  # small band: 26 text + 5 frames of 150 tokens
+    mod = sa.generate_block_tridiagonal_mask_mod(prompt_length=T, num_frames=n, token_per_frame=F, diag=1)
+    qi, ki = torch.arange(S)[:, None], torch.arange(S)[None, :]
+    out["band_small"] = np.packbits(mod(0, 0, qi, ki).numpy())
+    out["band_small_geom"] = np.array([T, n, 10, 15])
+    full = sa.generate_block_tridiagonal_mask_mod()
+    S2, rows = 17776, [226 + i * 1350 for i in range(13)]
+    keys = [torch.where(full(0, 0, torch.tensor(r), torch.arange(S2)))[0].numpy() for r in rows]
+    out["frame_keys"] = np.concatenate(keys).astype(np.int32)
+    out["frame_keys_off"] = np.cumsum([0] + [k.size for k in keys]).astype(np.int32)
+    idx = torch.arange(S2, dtype=torch.float64).view(1, 1, S2, 1)
+    out["process"] = sa.process(idx).reshape(-1).numpy().astype(np.int32)
+    out["process_back"] = sa.process_back(idx).reshape(-1).numpy().astype(np.int32)
+    return out
 
 
 def closure_vars(fn):
@@ -133,6 +161,7 @@ def main(root: str):
         out["unmerge_rowsum"] = un.sum(-1).reshape(-1).numpy()
         out["unmerge_proj"] = (un @ proj).reshape(-1).numpy()
         np.savez_compressed(HERE / f"{name}.npz", **out)
+    np.savez_compressed(HERE / "smart_layout.npz", **smart_layout(root))
     print("fixtures written to", HERE)
 
 

@@ -154,9 +154,7 @@ def test_merge_attention_against_oracle(cuda_device, full_merge):
     out = attn(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device)).float().cpu()
     plan = attn.merge_fn.plan
     # oracle composition on the same metric and split
-    kd, vd = k.to(cuda_device), v.to(cuda_device)
-    kv, vv = kd[:, :, text:].reshape(B * H, N, D), vd[:, :, text:].reshape(B * H, N, D)
-    metric = torch.cat((kv, kv.norm(dim=-1, keepdim=True), vv, vv.norm(dim=-1, keepdim=True)), -1).cpu()
+    metric = otome.kv_metric(k, v, text)
     a, b = plan.a_idx.cpu().numpy(), plan.b_idx.cpu().numpy()
     m = otome.match(metric, a, b, cfg["r"])
     def omerge(x):
@@ -180,3 +178,15 @@ def test_merge_attention_against_oracle(cuda_device, full_merge):
                                           1 / 8, 128, 128, kv_bias=bias)
     err = np.abs(out.numpy() - ref).max()
     assert err <= 2e-2, err
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_kv_metric_bit_exact(cuda_device, dtype):
+    g = torch.Generator().manual_seed(31)
+    base = torch.randn(2, 300, 3, 64, generator=g).to(dtype)
+    k = base.transpose(1, 2)                                            # strided [B, H, S, D]
+    v = (torch.randn(2, 3, 300, 64, generator=g) * 3).to(dtype)
+    got = kernels.tome_kv_metric(k.to(cuda_device), v.to(cuda_device), 26).cpu()
+    want = otome.kv_metric(k, v, 26)
+    assert got.shape == (6, 274, 130)
+    assert torch.equal(got, want)

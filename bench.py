@@ -128,6 +128,8 @@ def init_dist():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1 and not dist.is_initialized():
+        # rank 0's stdout carries exactly one JSON line: NCCL's own log lines go to stderr
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),

@@ -42,12 +42,13 @@ constexpr int kBM = 128;       // query rows per CTA
 constexpr int kD = 64;         // head dim handled by this kernel
 constexpr int kKS = 3;         // K stages
 constexpr int kVS = 2;         // V stages
-constexpr int kThreads = 384;  // 12 warps = 3 warpgroups
-// Register split: launched at 80 per thread (2 CTAs x 384 threads per SM);
-// warpgroup 0 (producer, MMA issuer, 2 idle warps) drops to 32, the two
-// softmax warpgroups rise to 104: 128*32 + 256*104 = 30720 = 384*80.
-constexpr uint32_t kRegsCtl = 32, kRegsSoftmax = 104;
-static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= kThreads * 80, "register split");
+constexpr int kThreads = 256;  // 8 warps = 2 warpgroups
+// Register split: launched at 128 per thread (2 CTAs x 256 threads per SM);
+// warpgroup 0 (producer, MMA issuer, 2 idle warps) drops to 32, the softmax
+// warpgroup (one thread per query row) rises to 224: 128*32 + 128*224 =
+// 32768 = 256*128.
+constexpr uint32_t kRegsCtl = 32, kRegsSoftmax = 224;
+static_assert(128 * kRegsCtl + 128 * kRegsSoftmax <= kThreads * 128, "register split");
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128, kColP = 192;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -187,13 +188,10 @@ struct Layout {
   static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + kKS * kKVBytes;
   static constexpr int kOffBias = kOffV + kVS * kKVBytes;
-  static constexpr int kOffXm = kOffBias + kVS * BN * 4;   // [2 parity][2 half][128] row max
-  static constexpr int kOffXl = kOffXm + 2 * 2 * kBM * 4;    // [2 half][128] row sum
-  static constexpr int kOffBar = kOffXl + 2 * kBM * 4;
+  static constexpr int kOffBar = kOffBias + kVS * BN * 4;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain,
-  //           x_full[2], x_end
-  static constexpr int kNumBars = 1 + 2 * kKS + 3 * kVS + 8;
+  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain
+  static constexpr int kNumBars = 1 + 2 * kKS + 3 * kVS + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
@@ -247,10 +245,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_p_full = bar_s_full + 16;
   const uint32_t bar_pv_full = bar_s_full + 24;
   const uint32_t bar_drain = bar_s_full + 32;
-  auto bar_x_full = [&](int par) { return bar_s_full + 40u + 8u * par; };
-  const uint32_t bar_x_end = bar_s_full + 56;
-  float* xm = reinterpret_cast<float*>(smem + L::kOffXm);
-  float* xl = reinterpret_cast<float*>(smem + L::kOffXl);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
 
@@ -266,13 +260,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar_b_full(s), 32);
     }
     mbar_init(bar_s_full, 1);
-    mbar_init(bar_s_empty, 256);
-    mbar_init(bar_p_full, 256);
+    mbar_init(bar_s_empty, 128);  // the softmax threads
+    mbar_init(bar_p_full, 128);
     mbar_init(bar_pv_full, 1);
     mbar_init(bar_drain, 1);
-    mbar_init(bar_x_full(0), 256);
-    mbar_init(bar_x_full(1), 256);
-    mbar_init(bar_x_end, 256);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -416,15 +407,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else {
     setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax
-    constexpr int HC = BN / 2;  // key columns per thread
+    // One thread per query row holds the row's BN scores of a block, so the
+    // block maximum needs no exchange between threads.
+    constexpr int NC = BN / 32;  // 32-column TMEM chunks of a block
     const int quarter = warp & 3;
-    const int chalf = (warp - 4) >> 2;  // column half of this warp
     const int row = quarter * 32 + lane;
     const uint32_t rhalf = static_cast<uint32_t>(row >> 6);  // row half (64-row mask blocks)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_addr + kColS + chalf * HC;
-    const uint32_t tO = tmem + lane_addr + kColO + chalf * (kD / 2);
-    const uint32_t tP = tmem + lane_addr + kColP + chalf * (HC / 2);
+    const uint32_t tS = tmem + lane_addr + kColS;
+    const uint32_t tO = tmem + lane_addr + kColO;
+    const uint32_t tP = tmem + lane_addr + kColP;
     const float sl2 = p.scale_log2;
     const f2 sl2x2 = mk2(sl2, sl2);
 
@@ -449,25 +441,24 @@ __global__ void __launch_bounds__(kThreads, 2)
         break;
       }
       tc_fence_after();
-      // Two x32 loads (not one x64: no single instruction may need more
-      // registers than the launch budget).
-      uint32_t r0[32], r1[32];
-      tmem_ld32(tS, r0);
-      if constexpr (HC == 64) tmem_ld32(tS + 32, r1);
-      tmem_wait_ld(r0);
-      if constexpr (HC == 64) tmem_wait_ld(r1);
-      auto r = [&](int e) -> uint32_t { return e < 32 ? r0[e] : r1[e - 32]; };
-      // This thread's half of S is in registers: the next QK^T may overwrite S.
+      // x32 loads (no single instruction may need more registers than the
+      // launch budget); one wait covers all of them.
+      uint32_t r[NC][32];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) tmem_ld32(tS + 32 * c, r[c]);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) tmem_wait_ld(r[c]);
+      // The row's scores are in registers: the next QK^T may overwrite S.
       tc_fence_before();
       mbar_arrive(bar_s_empty);
 
       const bool live = (rm >> rhalf) & 1u;
-      const int c0 = col * BN + chalf * HC;  // first key column of this half
-      const int valid = p.Sk - c0;           // valid columns of this half
-      bool fast = live && valid >= HC;       // warp-uniform without kRanges
+      const int c0 = col * BN;      // first key column of the block
+      const int valid = p.Sk - c0;  // valid columns of the block
+      bool fast = live && valid >= BN;
       if constexpr (kRanges)
-        fast = fast && ((c0 >= lo0 && c0 + HC <= hi0) || (c0 >= lo1 && c0 + HC <= hi1));
-      float t[HC];
+        fast = fast && ((c0 >= lo0 && c0 + BN <= hi0) || (c0 >= lo1 && c0 + BN <= hi1));
+      float t[BN];
       if constexpr (kBias) {
         const int sv = j % kVS;
         if (!__all_sync(0xffffffffu, mbar_wait(bar_b_full(sv), (j / kVS) & 1, abort_flag,
@@ -475,38 +466,37 @@ __global__ void __launch_bounds__(kThreads, 2)
           ok = false;
           break;
         }
-        const float* bb = sBias + sv * BN + chalf * HC;
+        const float* bb = sBias + sv * BN;
 #pragma unroll
-        for (int e = 0; e < HC; e += 2) {
+        for (int e = 0; e < BN; e += 2) {
           const float2 bv = *reinterpret_cast<const float2*>(bb + e);
-          const f2 x = fma2(mk2(__uint_as_float(r(e)), __uint_as_float(r(e + 1))), sl2x2,
-                            mk2(bv.x, bv.y));
+          const f2 x = fma2(mk2(__uint_as_float(r[e / 32][e % 32]), __uint_as_float(r[e / 32][e % 32 + 1])),
+                            sl2x2, mk2(bv.x, bv.y));
           t[e] = lo2(x);
           t[e + 1] = hi2(x);
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < HC; ++e) t[e] = __uint_as_float(r(e));
+        for (int e = 0; e < BN; ++e) t[e] = __uint_as_float(r[e / 32][e % 32]);
       }
       if (!fast) {
         if constexpr (kRanges) {
           const int a0 = lo0 - c0, b0 = hi0 - c0, a1 = lo1 - c0, b1 = hi1 - c0;
 #pragma unroll
-          for (int e = 0; e < HC; ++e)
+          for (int e = 0; e < BN; ++e)
             if (!(live && e < valid && ((e >= a0 && e < b0) || (e >= a1 && e < b1)))) t[e] = -INFINITY;
         } else {
 #pragma unroll
-          for (int e = 0; e < HC; ++e)
+          for (int e = 0; e < BN; ++e)
             if (!(live && e < valid)) t[e] = -INFINITY;
         }
       }
       // Under lazy rescaling the running max rarely moves, so P is computed
       // speculatively with the current running max while the block max is
-      // accumulated alongside (ALU work next to the MUFU work).  The pair then
-      // exchanges maxima; only if a row's max jumped past the threshold does
-      // the warp recompute P (the scores are still in registers) and rescale
-      // O.  A warp with a row that has not seen a live score yet takes the
-      // max-first order.
+      // accumulated alongside (ALU work next to the MUFU work); only if the
+      // row's max jumped past the threshold does the warp recompute P (the
+      // scores are still in registers) and rescale O.  A warp with a row that
+      // has not seen a live score yet takes the max-first order.
       const bool spec = __all_sync(0xffffffffu, m_run != -INFINITY);
       bool pv_done = (j == 0);
       // PV of the previous block must be done before P is overwritten and
@@ -533,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         rs = mk2(0.f, 0.f);
         float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < HC / 32; ++c) {
+        for (int c = 0; c < NC; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -560,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
           if (c == 0 && !wait_pv()) return false;
           tmem_st16(tP + c * 16, pk);
-          if (c + 1 < HC / 32) {
+          if (c + 1 < NC) {
             asm volatile("" : "+l"(rs.v));
 #pragma unroll
             for (int e = 0; e < 32; ++e) asm volatile("" : "+f"(t[(c + 1) * 32 + e]));
@@ -578,22 +568,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else {
         float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < HC / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
+        for (int i = 0; i < BN / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
         mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
       }
       if constexpr (!kBias) mx *= sl2;
-      // Exchange the half-row maxima of the pair (parity-buffered).
-      float* xbuf = xm + (j & 1) * 2 * kBM;
-      xbuf[chalf * kBM + row] = mx;
-      mbar_arrive(bar_x_full(j & 1));
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_x_full(j & 1), (j >> 1) & 1, abort_flag,
-                                              p.status, p.budget_ns))) {
-        ok = false;
-        break;
-      }
-      const float m_cand = fmaxf(mx, xbuf[(chalf ^ 1) * kBM + row]);
-      const bool upd = m_cand > m_run + kRescaleThreshold;
-      const float m_new = upd ? m_cand : m_run;
+      const bool upd = mx > m_run + kRescaleThreshold;
+      const float m_new = upd ? mx : m_run;
       const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
       const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
       const bool any_upd = __any_sync(0xffffffffu, upd);
@@ -608,12 +588,15 @@ __global__ void __launch_bounds__(kThreads, 2)
           ok = false;
           break;
         }
-        uint32_t orr[32];
-        tmem_ld32(tO, orr);
-        tmem_wait_ld(orr);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-        tmem_st32(tO, orr);
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t orr[32];
+          tmem_ld32(tO + 32 * c, orr);
+          tmem_wait_ld(orr);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+          tmem_st32(tO + 32 * c, orr);
+        }
       }
       l_run = l_run * alpha + (lo2(rs) + hi2(rs));
       m_run = m_new;
@@ -624,46 +607,43 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---------------------------------------------------------- epilogue
-    // Row sum = sum of the pair's partial sums.  O is read back 32 columns per
-    // thread, normalised by 1/l and stored.  A zero row sum gives
-    // 0 * inf = NaN, matching the reference; a tile with no live block never
-    // wrote O and stores NaN as well.
+    // O is read back 32 columns at a time, normalised by 1/l and stored.  A
+    // zero row sum gives 0 * inf = NaN, matching the reference; a tile with no
+    // live block never wrote O and stores NaN as well.
     const bool have_o =
         ok && j > 0 &&
         __all_sync(0xffffffffu,
                    mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status, p.budget_ns));
     if (have_o) tc_fence_after();
-    xl[chalf * kBM + row] = l_run;
-    mbar_arrive(bar_x_end);
-    const bool have_l = ok && __all_sync(0xffffffffu, mbar_wait(bar_x_end, 0, abort_flag, p.status,
-                                                                 p.budget_ns));
-    const float l_tot = l_run + (have_l ? xl[(chalf ^ 1) * kBM + row] : 0.f);
     const int qrow = q0 + row;
-    const float inv_l = 1.f / l_tot;
+    const float inv_l = 1.f / l_run;
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
                    2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
-                        static_cast<int64_t>(qrow) * p.o_ss + chalf * (kD / 2));
-    const bool write = (j == 0 || have_o) && have_l && !*abort_flag && qrow < p.Sq;
-    uint32_t orr[32];
-    if (have_o) {
-      tmem_ld32(tO, orr);
-      tmem_wait_ld(orr);
-    } else {
+                        static_cast<int64_t>(qrow) * p.o_ss);
+    const bool write = (j == 0 || have_o) && ok && !*abort_flag && qrow < p.Sq;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) orr[e] = 0u;
-    }
-    if (write) {
+    for (int c = 0; c < kD / 32; ++c) {
+      uint32_t orr[32];
+      if (have_o) {
+        tmem_ld32(tO + 32 * c, orr);
+        tmem_wait_ld(orr);
+      } else {
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        uint4 w;
-        uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
+        for (int e = 0; e < 32; ++e) orr[e] = 0u;
+      }
+      if (write) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float lo = __uint_as_float(orr[v * 8 + 2 * e]) * inv_l;
-          const float hi = __uint_as_float(orr[v * 8 + 2 * e + 1]) * inv_l;
-          pw[e] = kBF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float lo = __uint_as_float(orr[v * 8 + 2 * e]) * inv_l;
+            const float hi = __uint_as_float(orr[v * 8 + 2 * e + 1]) * inv_l;
+            pw[e] = kBF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+          }
+          reinterpret_cast<uint4*>(dst)[c * 4 + v] = w;
         }
-        reinterpret_cast<uint4*>(dst)[v] = w;
       }
     }
     tc_fence_before();

@@ -127,6 +127,23 @@ int32_t saf_mask_to_csr(const uint8_t* mask, int64_t BH, int32_t nbq, int32_t nb
                         int64_t stride_bh, int64_t stride_row, int32_t* row_ptr,
                         int32_t* col_idx, void* stream);
 
+/* Energy-threshold block selection (SparseGen_Plus's adaptive density).
+ * in: fp64 [BH, nbq, nbk] contiguous -- the estimated attention mass per key
+ * block when is_mass != 0, else mean-pooled scores (saf_pool_topk's scores)
+ * turned into mass_j = n_j * exp(scale * s_j - max scale * s) with n_j the
+ * tokens of key block j (block_n, last block Sk - (nbk-1)*block_n).  Per
+ * row: sort descending (ties to the lower column), keep the prefix that
+ * ends before the first position where the fp64 running sum reaches
+ * threshold * total (all if none), clamped to [min_retain, max_retain];
+ * rows / columns < text_blocks forced.  Writes the uint8 block mask
+ * [BH, nbq, nbk] (saf_mask_to_csr makes the CSR) and, if mass_out is not
+ * null, the mass used.  nbk <= 1024.
+ * Replaces: transfer_attn_to_mask(mode="energy") (SparseGen_Plus.py:12-84). */
+int32_t saf_energy_select(const double* in, int32_t is_mass, int64_t BH, int32_t nbq, int32_t nbk,
+                          int32_t block_n, int64_t Sk, double scale, double threshold,
+                          int32_t min_retain, int32_t max_retain, int32_t text_blocks,
+                          double* mass_out, uint8_t* mask, void* stream);
+
 /* ---- (2) block-sparse attention -------------------------------------
  * o[b,h,i,:] = sum_{j live} softmax_j(sm_scale * q_i . k_j + bias_j) v_j
  * over the key blocks listed in the CSR row of query block i / block_m.

@@ -109,6 +109,8 @@ SIGNATURES = {
     "saf_pool_topk_workspace_bytes": (_SZ, [_PT4, _PT4, _PCFG]),
     "saf_pool_topk": (_I32, [_PT4, _PT4, _PCFG, _P, _P, _P, _P, _P, _SZ, _P]),
     "saf_pool_topk_noalloc": (_I32, [_PT4, _PT4, _PCFG, _P, _P, _P, _P, _P]),
+    "saf_energy_select": (_I32, [_P, _I32, _I64, _I32, _I32, _I32, _I64, ctypes.c_double, ctypes.c_double,
+                                 _I32, _I32, _I32, _P, _P, _P]),
     "saf_mask_to_csr": (_I32, [_P, _I64, _I32, _I32, _I64, _I64, _P, _P, _P]),
     "saf_bsa_fwd": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I64, _F32, _I32,
                            _P]),

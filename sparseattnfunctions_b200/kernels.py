@@ -147,6 +147,29 @@ def pool_topk(q: torch.Tensor, k: torch.Tensor, *, block_m: int, block_n: int, t
                     dense_rows=min(text_blocks_q, nbq))
 
 
+def energy_select(x: torch.Tensor, *, threshold: float, min_retain: int, max_retain: int,
+                  text_blocks: int = 0, is_mass: bool = True, scale: float = 1.0, block_n: int = 0,
+                  Sk: int = 0, return_mass: bool = False):
+    """Energy-threshold block mask from ``x [B, H, nbq, nbk]`` (fp64 block
+    mass when ``is_mass``, else mean-pooled scores turned into mass with
+    ``scale``, ``block_n`` and ``Sk``).  Returns the uint8 mask
+    ``[B, H, nbq, nbk]`` (and the fp64 mass used when ``return_mass``)."""
+    dev = _require_cuda(x)
+    if x.dim() != 4:
+        raise ValueError("expected a [B, H, nbq, nbk] tensor")
+    x = x.to(torch.float64).contiguous()
+    B, H, nbq, nbk = x.shape
+    mask = torch.empty(B, H, nbq, nbk, dtype=torch.uint8, device=dev)
+    mass = torch.empty_like(x) if return_mass else None
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_energy_select(x.data_ptr(), int(is_mass), B * H, nbq, nbk, int(block_n), int(Sk),
+                                           float(scale), float(threshold), int(min_retain), int(max_retain),
+                                           int(text_blocks), mass.data_ptr() if mass is not None else None,
+                                           mask.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_energy_select", rc)
+    return (mask, mass) if return_mass else mask
+
+
 def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int, dense_rows: int = 0) -> BlockCSR:
     """Dense boolean block mask ``[B, H, nbq, nbk]`` -> ``BlockCSR``.  ``dense_rows``
     tells ``bsa_fwd`` how many leading row blocks have the longest lists."""

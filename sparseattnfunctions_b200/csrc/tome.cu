@@ -55,15 +55,22 @@ struct ScoreParams {
   uint64_t budget_ns;
 };
 
-struct ScoreLayout {
+constexpr int kResChunks = 4;  // A-resident variant: up to 4 K chunks (C <= 256)
+
+// kRes = false: every stage holds an A and a B chunk (A re-streamed per
+// N tile; any C).  kRes = true: the CTA's A rows (at most kResChunks K
+// chunks) are loaded once and stay in shared memory, the stages hold B only.
+template <bool kRes>
+struct ScoreLayoutT {
   static constexpr int kABytes = kTM * kTK * 2;  // 16 KB
   static constexpr int kBBytes = kTN * kTK * 2;  // 32 KB
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kOffRing = 0;
-  static constexpr int kOffCand = kStages * kStageBytes;            // [2][128][8] (val, idx)
+  static constexpr int kStageBytes = kRes ? kBBytes : kABytes + kBBytes;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffRing = kRes ? kResChunks * kABytes : 0;
+  static constexpr int kOffCand = kOffRing + kStages * kStageBytes;  // [2][128][8] (val, idx)
   static constexpr int kOffBar = kOffCand + 2 * kTM * kCand * 8;
-  // full[S], empty[S], acc_full[2], acc_empty[2], drain, xend
-  static constexpr int kNumBars = 2 * kStages + 6;
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain, xend, a_full
+  static constexpr int kNumBars = 2 * kStages + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kDynSmem = kOffMisc + 16 + 1024;
 };
@@ -86,11 +93,11 @@ __device__ __forceinline__ void cand_insert(float (&v)[kCand], int (&ix)[kCand],
 }
 
 // grid (ceil(Ns/128), B).  One CTA per SM (TMEM: two 256-column accumulators).
-template <bool kBF16>
+template <bool kBF16, bool kRes>
 __global__ void __launch_bounds__(kScoreThreads, 1)
     tome_score_kernel(const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_b, const ScoreParams p) {
-  using L = ScoreLayout;
+  using L = ScoreLayoutT<kRes>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -105,6 +112,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   auto bar_acc_empty = [&](int i) { return bar0 + 8u * (2 * kStages + 2 + i); };
   const uint32_t bar_drain = bar0 + 8u * (2 * kStages + 4);
   const uint32_t bar_xend = bar0 + 8u * (2 * kStages + 5);
+  const uint32_t bar_a = bar0 + 8u * (2 * kStages + 6);  // resident A landed (kRes)
+  const uint32_t sA = smem_u32(smem + L::kOffA);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
 
@@ -119,6 +128,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     }
     mbar_init(bar_drain, 1);
     mbar_init(bar_xend, 256);
+    mbar_init(bar_a, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_a);
@@ -137,6 +147,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     // ------------------------------------------------------------ producer
     int issued = 0;
     if (lane == 0) {
+      if constexpr (kRes) {
+        mbar_arrive_expect_tx(bar_a, k_chunks * L::kABytes);
+        for (int kc = 0; kc < k_chunks; ++kc) tma_load_3d(sA + kc * L::kABytes, &tm_a, bar_a, kc * kTK, m0, b);
+      }
       for (int nt = 0; nt < n_tiles; ++nt) {
         for (int kc = 0; kc < k_chunks; ++kc, ++issued) {
           const int s = issued % kStages;
@@ -144,12 +158,17 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           if (!mbar_wait(bar_empty(s), ph ^ 1, abort_flag, p.status, p.budget_ns)) break;
           const uint32_t st = ring + s * L::kStageBytes;
           mbar_arrive_expect_tx(bar_full(s), L::kStageBytes);
-          tma_load_3d(st, &tm_a, bar_full(s), kc * kTK, m0, b);
-          tma_load_3d(st + L::kABytes, &tm_b, bar_full(s), kc * kTK, nt * kTN, b);
+          if constexpr (kRes) {
+            tma_load_3d(st, &tm_b, bar_full(s), kc * kTK, nt * kTN, b);
+          } else {
+            tma_load_3d(st, &tm_a, bar_full(s), kc * kTK, m0, b);
+            tma_load_3d(st + L::kABytes, &tm_b, bar_full(s), kc * kTK, nt * kTN, b);
+          }
         }
         if (*abort_flag) break;
       }
-      // drain: wait for the last load of every stage
+      // drain: wait for the last load of every stage (and the resident A)
+      if constexpr (kRes) mbar_drain(bar_a, 0, p.status);
       for (int s = 0; s < kStages && s < issued; ++s) {
         const int last = s + ((issued - 1 - s) / kStages) * kStages;
         mbar_drain(bar_full(s), (last / kStages) & 1, p.status);
@@ -162,6 +181,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       constexpr uint32_t kIdesc = idesc_f16(kTM, kTN, kBF16, false, false);
       int used = 0;
       bool ok = true;
+      if constexpr (kRes) ok = mbar_wait(bar_a, 0, abort_flag, p.status, p.budget_ns);
       for (int nt = 0; nt < n_tiles && ok; ++nt) {
         const int buf = nt & 1;
         if (!mbar_wait(bar_acc_empty(buf), ((nt >> 1) & 1) ^ 1, abort_flag, p.status,
@@ -179,10 +199,12 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           }
           tc_fence_after();
           const uint32_t st = ring + s * L::kStageBytes;
+          const uint32_t a_chunk = kRes ? sA + kc * L::kABytes : st;
+          const uint32_t b_chunk = kRes ? st : st + L::kABytes;
 #pragma unroll
           for (int kk = 0; kk < kTK / 16; ++kk) {
-            const uint64_t ad = sdesc_sw128(st + kk * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(st + L::kABytes + kk * 32, 16, 1024);
+            const uint64_t ad = sdesc_sw128(a_chunk + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b_chunk + kk * 32, 16, 1024);
             tc_mma_ss(acc, ad, bd, kIdesc, (kc > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(bar_empty(s));
@@ -816,15 +838,20 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   ScoreParams sp{static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd), static_cast<int>(Cp),
                  na, rinv, ci, cv, status, wait_budget_ns()};
   dim3 sg(static_cast<unsigned>((Ns + kTM - 1) / kTM), static_cast<unsigned>(B));
-  const int smem = ScoreLayout::kDynSmem;
-  if (bf16) {
-    SAF_CUDA_TRY(cudaFuncSetAttribute(tome_score_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    tome_score_kernel<true><<<sg, kScoreThreads, smem, st>>>(ma, mb, sp);
-  } else {
-    SAF_CUDA_TRY(cudaFuncSetAttribute(tome_score_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    tome_score_kernel<false><<<sg, kScoreThreads, smem, st>>>(ma, mb, sp);
-  }
-  SAF_CUDA_TRY(cudaGetLastError());
+  // narrow metrics (per-head [k, |k|, v, |v|]) keep A resident; wide ones stream it
+  const bool res = Cp / kTK <= kResChunks;
+  auto launch = [&](auto kern, int smem) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<sg, kScoreThreads, smem, st>>>(ma, mb, sp);
+    return cudaGetLastError();
+  };
+  if (bf16)
+    SAF_CUDA_TRY(res ? launch(tome_score_kernel<true, true>, ScoreLayoutT<true>::kDynSmem)
+                     : launch(tome_score_kernel<true, false>, ScoreLayoutT<false>::kDynSmem));
+  else
+    SAF_CUDA_TRY(res ? launch(tome_score_kernel<false, true>, ScoreLayoutT<true>::kDynSmem)
+                     : launch(tome_score_kernel<false, false>, ScoreLayoutT<false>::kDynSmem));
 
   // 3. exact fp64 re-score of the candidates
   ExactParams ep{A, Bm, na, nb, ci, cv, static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd),

@@ -46,6 +46,56 @@ struct PoolOperand {
   double* out;  // [B*H, nb, D]
 };
 
+// One warp per (head, block): lanes hold 16-byte column chunks of 32 / lpr
+// rows at a time (lpr = lanes per row, a power of two), accumulate in fp64,
+// and combine the row groups with xor shuffles -- no shared memory and no
+// block barrier, so the many small blocks cost no per-CTA synchronisation.
+// grid (ceil(B*H*max nb / 8), 1, 2): z = 0 pools q, z = 1 pools k.
+template <typename T>
+__global__ void __launch_bounds__(256) pool_mean_warp_kernel(PoolOperand q_op, PoolOperand k_op, int H,
+                                                             int D, int BH, int lpr_log2) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int U = 8;  // row loads in flight per lane
+  const PoolOperand& op = blockIdx.z == 0 ? q_op : k_op;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  if (wid >= static_cast<int64_t>(BH) * op.nb) return;
+  const int g = static_cast<int>(wid / op.nb), blk = static_cast<int>(wid % op.nb);
+  const int b = g / H, h = g % H;
+  const int lpr = 1 << lpr_log2, rpi = 32 >> lpr_log2;
+  const int c = lane & (lpr - 1), ro = lane >> lpr_log2;
+  const int r0 = blk * op.block;
+  const int nrows = min(op.block, op.S - r0);
+  const T* base = static_cast<const T*>(op.x) + static_cast<int64_t>(b) * op.sb +
+                  static_cast<int64_t>(h) * op.sh + static_cast<int64_t>(r0) * op.ss + c * VEC;
+  double acc[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) acc[e] = 0.0;
+  for (int r = ro; r < nrows; r += rpi * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int rr = r + u * rpi;
+      v[u] = rr < nrows ? __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(rr) * op.ss))
+                        : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const T* pv = reinterpret_cast<const T*>(&v[u]);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] += to_f64(pv[e]);
+    }
+  }
+  for (int m = lpr; m < 32; m <<= 1)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], m);
+  if (ro == 0) {
+    double* o = op.out + (static_cast<int64_t>(g) * op.nb + blk) * D + c * VEC;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) o[e] = acc[e] / static_cast<double>(nrows);
+  }
+}
+
 // grid (max nb, B*H, 2): z = 0 pools q, z = 1 pools k.  Mean over the rows of
 // one block in fp64.  Each thread owns one 16-byte column chunk and issues all
 // of its row loads before accumulating, so a CTA keeps the whole block in
@@ -113,21 +163,28 @@ __device__ __forceinline__ bool better(double a, int ia, double b, int ib) {
   return a > b || (a == b && ia < ib);
 }
 
-// grid (B*H, ceil(nbq / 8)), 256 threads; one warp per row block.  The key
-// means of the head are staged in shared memory 32 dims at a time; every lane
-// owns columns lane + 32m (m < M) and accumulates their fp64 scores with d
-// ascending.  The top-k is k rounds of a warp arg-max (ties -> lower column).
+// grid (B*H, ceil(nbq / 32)), 256 threads; each warp owns kRowsPerWarp
+// consecutive row blocks, so every key mean staged in shared memory (32 dims
+// at a time) serves four rows.  Every lane owns columns lane + 32m (m < M)
+// and accumulates their fp64 scores with d ascending (separate multiply and
+// add, no contraction).  The top-k is k rounds of a warp arg-max (ties ->
+// lower column).
+constexpr int kRowsPerWarp = 4;
+constexpr int kRowsPerCta = 8 * kRowsPerWarp;
+
 template <int M>
 __global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
-  extern __shared__ double ks[];  // [nbk][kDChunk+1] then [8][kDChunk+1]
+  extern __shared__ double ks[];  // [nbk][kDChunk+1] then [32][kDChunk+1]
   double* qs = ks + a.nbk * (kDChunk + 1);
   const int g = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.y * 8 + warp;
+  const int row0 = blockIdx.y * kRowsPerCta + warp * kRowsPerWarp;
 
-  double sc[M];
+  double sc[kRowsPerWarp][M];
 #pragma unroll
-  for (int m = 0; m < M; ++m) sc[m] = 0.0;
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int m = 0; m < M; ++m) sc[i][m] = 0.0;
 
   const double* kb = a.kbar + static_cast<int64_t>(g) * a.nbk * a.D;
   const double* qb = a.qbar + static_cast<int64_t>(g) * a.nbq * a.D;
@@ -137,86 +194,93 @@ __global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
       const int j = idx / kDChunk, d = idx % kDChunk;
       ks[j * (kDChunk + 1) + d] = kb[static_cast<int64_t>(j) * a.D + d0 + d];
     }
-    {
-      const int r = threadIdx.x / kDChunk, d = threadIdx.x % kDChunk;  // 8 x 32
-      const int rr = blockIdx.y * 8 + r;
+    for (int idx = threadIdx.x; idx < kRowsPerCta * kDChunk; idx += blockDim.x) {
+      const int r = idx / kDChunk, d = idx % kDChunk;
+      const int rr = blockIdx.y * kRowsPerCta + r;
       qs[r * (kDChunk + 1) + d] = rr < a.nbq ? qb[static_cast<int64_t>(rr) * a.D + d0 + d] : 0.0;
     }
     __syncthreads();
-    const double* qr = qs + warp * (kDChunk + 1);
+    const double* qr = qs + warp * kRowsPerWarp * (kDChunk + 1);
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       const int j = lane + 32 * m;
       if (j < a.nbk) {
-        double s = sc[m];
         const double* kr = ks + j * (kDChunk + 1);
-#pragma unroll 8
-        for (int d = 0; d < kDChunk; ++d) s = __dadd_rn(s, __dmul_rn(qr[d], kr[d]));
-        sc[m] = s;
-      }
-    }
-  }
-  if (row >= a.nbq) return;
-
-  const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
-  uint32_t forced = 0, eligible = 0, sel = 0;  // bit m <-> column lane + 32m
-  const bool text_row = row < a.text_q;
+#pragma unroll 4
+        for (int d = 0; d < kDChunk; ++d) {
+          const double kv = kr[d];
 #pragma unroll
-  for (int m = 0; m < M; ++m) {
-    const int j = lane + 32 * m;
-    if (j < a.nbk) {
-      const bool f = text_row || j < a.text_k || (a.force_diag && j == row);
-      if (f) forced |= 1u << m;
-      if (!(f && a.forced_inside)) eligible |= 1u << m;
-    }
-  }
-  int nforced = 0;
-#pragma unroll
-  for (int m = 0; m < M; ++m) nforced += __popc(__ballot_sync(0xffffffffu, (forced >> m) & 1u));
-  int krem = a.forced_inside ? a.topk - nforced : a.topk;
-  if (text_row) krem = 0;
-  for (int round = 0; round < krem; ++round) {
-    double best = -INFINITY;
-    int bj = 0x7fffffff;
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      if (((eligible & ~sel) >> m) & 1u) {
-        const int j = lane + 32 * m;
-        if (better(sc[m], j, best, bj)) {
-          best = sc[m];
-          bj = j;
+          for (int i = 0; i < kRowsPerWarp; ++i)
+            sc[i][m] = __dadd_rn(sc[i][m], __dmul_rn(qr[i * (kDChunk + 1) + d], kv));
         }
       }
     }
+  }
+
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const double ob = __shfl_xor_sync(0xffffffffu, best, off);
-      const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
-      if (better(ob, oj, best, bj)) {
-        best = ob;
-        bj = oj;
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int row = row0 + i;
+    if (row >= a.nbq) break;
+    const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
+    uint32_t forced = 0, eligible = 0, sel = 0;  // bit m <-> column lane + 32m
+    const bool text_row = row < a.text_q;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int j = lane + 32 * m;
+      if (j < a.nbk) {
+        const bool f = text_row || j < a.text_k || (a.force_diag && j == row);
+        if (f) forced |= 1u << m;
+        if (!(f && a.forced_inside)) eligible |= 1u << m;
       }
     }
-    if (bj == 0x7fffffff) break;  // no candidate left
-    if ((bj & 31) == lane) sel |= 1u << (bj >> 5);
-  }
-  sel |= forced;
-  int base = 0;
+    int nforced = 0;
 #pragma unroll
-  for (int m = 0; m < M; ++m) {
-    const uint32_t bal = __ballot_sync(0xffffffffu, (sel >> m) & 1u);
-    if ((sel >> m) & 1u) {
-      const int pos = base + __popc(bal & ((1u << lane) - 1u));
-      a.padded[rbase + pos] = lane + 32 * m;
+    for (int m = 0; m < M; ++m) nforced += __popc(__ballot_sync(0xffffffffu, (forced >> m) & 1u));
+    int krem = a.forced_inside ? a.topk - nforced : a.topk;
+    if (text_row) krem = 0;
+    for (int round = 0; round < krem; ++round) {
+      double best = -INFINITY;
+      int bj = 0x7fffffff;
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        if (((eligible & ~sel) >> m) & 1u) {
+          const int j = lane + 32 * m;
+          if (better(sc[i][m], j, best, bj)) {
+            best = sc[i][m];
+            bj = j;
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+        if (better(ob, oj, best, bj)) {
+          best = ob;
+          bj = oj;
+        }
+      }
+      if (bj == 0x7fffffff) break;  // no candidate left
+      if ((bj & 31) == lane) sel |= 1u << (bj >> 5);
     }
-    base += __popc(bal);
-    const int j = lane + 32 * m;
-    if (j < a.nbk) {
-      if (a.mask_out) a.mask_out[rbase + j] = (sel >> m) & 1u;
-      if (a.score_out) a.score_out[rbase + j] = sc[m];
+    sel |= forced;
+    int base = 0;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (sel >> m) & 1u);
+      if ((sel >> m) & 1u) {
+        const int pos = base + __popc(bal & ((1u << lane) - 1u));
+        a.padded[rbase + pos] = lane + 32 * m;
+      }
+      base += __popc(bal);
+      const int j = lane + 32 * m;
+      if (j < a.nbk) {
+        if (a.mask_out) a.mask_out[rbase + j] = (sel >> m) & 1u;
+        if (a.score_out) a.score_out[rbase + j] = sc[i][m];
+      }
     }
+    if (lane == 0) a.counts[static_cast<int64_t>(g) * a.nbq + row] = base;
   }
-  if (lane == 0) a.counts[static_cast<int64_t>(g) * a.nbq + row] = base;
 }
 
 // grid (B*H, ceil(nbq / 8)), 256 threads.  Every CTA redoes the (small)
@@ -342,6 +406,15 @@ int32_t launch_pool_t(const saf_tensor4* q, const saf_tensor4* k, int bm, int bn
   const size_t smem = static_cast<size_t>(groups) * D * sizeof(double);
   PoolOperand qo{q->data, static_cast<int>(q->S), q->stride_b, q->stride_h, q->stride_s, bm, nbq, qbar};
   PoolOperand ko{k->data, static_cast<int>(k->S), k->stride_b, k->stride_h, k->stride_s, bn, nbk, kbar};
+  const int BH = static_cast<int>(q->B * q->H);
+  if (vpr <= 32 && (vpr & (vpr - 1)) == 0) {  // lanes per row: a power of two
+    int lg = 0;
+    while ((1 << lg) < vpr) ++lg;
+    const int64_t pairs = static_cast<int64_t>(BH) * (nbq > nbk ? nbq : nbk);
+    dim3 wgrid(static_cast<unsigned>((pairs + 7) / 8), 1, 2);
+    pool_mean_warp_kernel<T><<<wgrid, 256, 0, st>>>(qo, ko, static_cast<int>(q->H), D, BH, lg);
+    return SAF_OK;
+  }
   dim3 grid(nbq > nbk ? nbq : nbk, static_cast<unsigned>(q->B * q->H), 2);
   // rows per thread per pass: the whole block in one pass when it fits in 8
   const int bmax = bm > bn ? bm : bn;
@@ -377,10 +450,10 @@ int32_t pool_dispatch(const saf_tensor4* q, const saf_tensor4* k, int bm, int bn
 
 template <int M>
 int32_t launch_score(const SelectArgs& a, int64_t BH, cudaStream_t st) {
-  const size_t smem = (static_cast<size_t>(a.nbk) + 8) * (kDChunk + 1) * sizeof(double);
+  const size_t smem = (static_cast<size_t>(a.nbk) + kRowsPerCta) * (kDChunk + 1) * sizeof(double);
   SAF_CUDA_TRY(cudaFuncSetAttribute(score_topk_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
-  dim3 grid(static_cast<unsigned>(BH), (a.nbq + 7) / 8);
+  dim3 grid(static_cast<unsigned>(BH), (a.nbq + kRowsPerCta - 1) / kRowsPerCta);
   score_topk_kernel<M><<<grid, 256, smem, st>>>(a);
   return SAF_OK;
 }

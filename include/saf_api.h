@@ -69,6 +69,12 @@ typedef struct saf_select_cfg {
 
 /* ---- library / device ---------------------------------------------- */
 
+/* Self-test of failure detection: launches a one-warp kernel that waits on an
+ * mbarrier nothing arrives on; after budget_ns (at most 10 s) the wait gives
+ * up and sets SAF_DEV_TIMEOUT, exactly as a stuck wait in any kernel does.
+ * Test hook with no reference counterpart. */
+int32_t saf_selftest_timeout(uint64_t budget_ns, void* stream);
+
 int32_t saf_abi_version(void);
 const char* saf_status_string(int32_t status);
 /* SAF_OK when `device` is an sm_100 GPU the kernels were built for. */

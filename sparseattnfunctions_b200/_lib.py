@@ -106,6 +106,7 @@ SIGNATURES = {
     "saf_set_wait_budget_ns": (None, [_U64]),
     "saf_get_wait_budget_ns": (_U64, []),
     "saf_read_device_status": (_I32, [_I32, ctypes.POINTER(ctypes.c_uint32), _I32]),
+    "saf_selftest_timeout": (_I32, [_U64, _P]),
     "saf_pool_topk_workspace_bytes": (_SZ, [_PT4, _PT4, _PCFG]),
     "saf_pool_topk": (_I32, [_PT4, _PT4, _PCFG, _P, _P, _P, _P, _P, _SZ, _P]),
     "saf_pool_topk_noalloc": (_I32, [_PT4, _PT4, _PCFG, _P, _P, _P, _P, _P]),

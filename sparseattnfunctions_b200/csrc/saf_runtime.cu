@@ -86,6 +86,22 @@ int32_t bind_device_of(const void* ptr) {
   return SAF_OK;
 }
 
+namespace {
+// Waits on an mbarrier that nothing ever arrives on: the bounded wait gives
+// up after the budget and records SAF_DEV_TIMEOUT, as every kernel's waits do.
+__global__ void selftest_timeout_kernel(unsigned int* status, uint64_t budget_ns) {
+  __shared__ alignas(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait(smem_u32(&bar), 0, &abort_flag, status, budget_ns);
+  __syncthreads();
+}
+}  // namespace
 }  // namespace saf
 
 extern "C" {
@@ -120,6 +136,15 @@ int32_t saf_device_check(int32_t device) {
 
 void saf_set_wait_budget_ns(uint64_t ns) { g_wait_budget_ns.store(ns); }
 uint64_t saf_get_wait_budget_ns(void) { return g_wait_budget_ns.load(); }
+
+int32_t saf_selftest_timeout(uint64_t budget_ns, void* stream) {
+  unsigned int* st = saf::device_status_ptr();
+  if (st == nullptr) return SAF_ERR_CUDA;
+  if (budget_ns > 10000000000ull) return SAF_ERR_ARG;  // at most 10 s
+  saf::selftest_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(st, budget_ns);
+  SAF_CUDA_TRY(cudaGetLastError());
+  return SAF_OK;
+}
 
 int32_t saf_read_device_status(int32_t device, uint32_t* flags_out, int32_t clear) {
   if (flags_out == nullptr) return SAF_ERR_ARG;

@@ -10,6 +10,7 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 GPU and the built libsaf.so")
+    config.addinivalue_line("markers", "expects_device_status: the test sets and checks the device status flags")
 
 
 @pytest.fixture(scope="session")

@@ -258,17 +258,20 @@ int32_t saf_tome_unmerge(const void* y, void* out, int32_t dtype, int64_t B, int
                          int64_t o_stride_n, int32_t text_len, int64_t N, const int32_t* token_map,
                          void* stream);
 
-/* Token permutation of [B, H, S, D] tensors (element strides, D
- * contiguous): out[g, s, :] = x[g, perm[s], :] for the flat heads
- * g = b*H + h listed in heads[0..n_heads) (every head when heads is null).
- * perm entries outside [0, S) or heads outside [0, B*H) set
- * SAF_DEV_BADINDEX in the device status word and are skipped.
+/* Token permutation / padding of [B, H, S, D] tensors (element strides, D
+ * contiguous) into [B, H, S_out, D]: out[g, s, :] = x[g, perm[s], :] for
+ * s < S_out, a zero row where perm[s] == -1, for the flat heads g = b*H + h
+ * listed in heads[0..n_heads) (every head when heads is null).  Other perm
+ * entries outside [0, S) or heads outside [0, B*H) set SAF_DEV_BADINDEX in
+ * the device status word and are skipped.
  * Replaces: process / process_back of SmartAttention (SmartAttention.py:
- * 16-41), the (t, h, w) <-> (h, w, t) reordering of the video tokens. */
+ * 16-41), the (t, h, w) <-> (h, w, t) reordering of the video tokens, and
+ * preprocess / process_out_back of SildingTileAttention
+ * (SildingTileAttention.py:106-136) with every tile padded to a block. */
 int32_t saf_permute_tokens(const void* x, void* out, int32_t dtype, int64_t B, int64_t H, int64_t S,
-                           int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss, int64_t o_sb,
-                           int64_t o_sh, int64_t o_ss, const int32_t* perm, const int32_t* heads,
-                           int64_t n_heads, void* stream);
+                           int64_t S_out, int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss,
+                           int64_t o_sb, int64_t o_sh, int64_t o_ss, const int32_t* perm,
+                           const int32_t* heads, int64_t n_heads, void* stream);
 
 /* Ulysses sequence <-> head layout for the all-to-all of sequence-sharded
  * attention.  Sequence-sharded tensors are [B, s, H, D] (element strides

@@ -125,7 +125,7 @@ SIGNATURES = {
                               _I64, _I32, ctypes.POINTER(TomePlan), _P]),
     "saf_tome_unmerge": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I64, _P, _P]),
     "saf_permute_tokens": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
-                                  _I64, _P, _P, _I64, _P]),
+                                  _I64, _I64, _P, _P, _I64, _P]),
     "saf_ulysses_pack": (_I32, [_P, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P,
                                 _P]),
     "saf_ulysses_unpack": (_I32, [_P, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32,

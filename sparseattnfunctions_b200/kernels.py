@@ -247,20 +247,22 @@ def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm
 
 def permute_tokens(x: torch.Tensor, perm: torch.Tensor, heads: Optional[torch.Tensor] = None,
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``out[b, h, s] = x[b, h, perm[s]]`` for ``[B, H, S, D]`` tensors, for
-    the flat heads ``b*H + h`` in ``heads`` (int32; all heads when None;
-    other heads of ``out`` are left untouched)."""
+    """``out[b, h, s] = x[b, h, perm[s]]`` for ``[B, H, S, D]`` tensors,
+    ``s < len(perm)`` (``perm[s] == -1`` gives a zero row), for the flat heads
+    ``b*H + h`` in ``heads`` (int32; all heads when None; other heads of
+    ``out`` are left untouched)."""
     dev = _require_cuda(x, perm)
     x = _d_last(x)
     if x.dim() != 4 or x.dtype not in _DTYPES:
         raise ValueError("expected a [B, H, S, D] bf16 / f16 / f32 tensor")
     B, H, S, D = x.shape
-    if perm.dtype != torch.int32 or perm.numel() != S or not perm.is_contiguous():
-        raise ValueError(f"perm must be a contiguous int32 tensor of {S} entries")
+    if perm.dtype != torch.int32 or perm.dim() != 1 or not perm.is_contiguous():
+        raise ValueError("perm must be a contiguous 1-D int32 tensor")
+    S_out = perm.numel()
     if out is None:
-        out = torch.empty_like(x)
-    if out.shape != x.shape or out.dtype != x.dtype or out.stride(-1) != 1:
-        raise ValueError("out must match x in shape and dtype, D contiguous")
+        out = torch.empty(B, H, S_out, D, dtype=x.dtype, device=dev)
+    if tuple(out.shape) != (B, H, S_out, D) or out.dtype != x.dtype or out.stride(-1) != 1:
+        raise ValueError(f"out must be [{B}, {H}, {S_out}, {D}] of x's dtype, D contiguous")
     hp, nh = None, 0
     if heads is not None:
         _require_cuda(heads)
@@ -270,7 +272,7 @@ def permute_tokens(x: torch.Tensor, perm: torch.Tensor, heads: Optional[torch.Te
         if nh == 0:
             return out
     with torch.cuda.device(dev):
-        rc = _lib.load().saf_permute_tokens(x.data_ptr(), out.data_ptr(), _DTYPES[x.dtype], B, H, S, D,
+        rc = _lib.load().saf_permute_tokens(x.data_ptr(), out.data_ptr(), _DTYPES[x.dtype], B, H, S, S_out, D,
                                             x.stride(0), x.stride(1), x.stride(2), out.stride(0),
                                             out.stride(1), out.stride(2), perm.data_ptr(), hp, nh,
                                             _stream_ptr(dev))

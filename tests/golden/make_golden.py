@@ -17,6 +17,9 @@ Fixtures
   energy_masks.npz  transfer_attn_to_mask(mode="energy") (SparseGen_Plus.py:12-84)
   tome_*.npz        bipartite_soft_matching_video + merge / unmerge
                     (utils/merge_unmerge.py:34-154), fp64 metric
+  sta_layout.npz    SildingTileAttention's tile-window mask_mod (small and
+                    CogVideoX-2B configs) and its preprocess token order
+                    (SildingTileAttention.py:18-136)
   smart_layout.npz  SmartAttention's frame-band mask_mod on a small geometry,
                     its per-frame key sets at CogVideoX-2B size, and the
                     process / process_back token orders (SmartAttention.py:
@@ -48,6 +51,45 @@ def import_reference(root: str):
     from special_attentions.utils import block_sparse_attn_kernel, merge_unmerge
 
     return block_sparse_attn_kernel, SparseGen_Plus, merge_unmerge
+
+
+def sta_layout(root: str):
+    """Evaluates SildingTileAttention's mask_mod and preprocess on the CPU.
+    The module builds a CUDA block mask when imported, so its function and
+    class definitions are taken from the source text and executed alone."""
+    import ast
+    import torch
+    from einops import rearrange
+
+    src = Path(root, "special_attentions", "SildingTileAttention.py").read_text()
+    tree = ast.parse(src)
+    keep = [n for n in tree.body if isinstance(n, (ast.FunctionDef, ast.ClassDef)) and
+            n.name in ("generate_sta_mask", "SildingTileAttention")]
+    ns = {"torch": torch, "rearrange": rearrange, "Tuple": tuple, "IntTensor": torch.Tensor,
+          "BoolTensor": torch.Tensor}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), "sta", "exec"), ns)
+    out = {}
+    # small configuration: full token-level mask
+    canvas, tile, kern, text = (4, 6, 9), (2, 3, 3), (1, 3, 3), 10
+    mod = ns["generate_sta_mask"](canvas, kern, tile, text)
+    S = text + canvas[0] * canvas[1] * canvas[2]
+    qi, ki = torch.arange(S)[:, None], torch.arange(S)[None, :]
+    out["small_mask"] = np.packbits(mod(0, 0, qi, ki).numpy())
+    out["small_cfg"] = np.array([*canvas, *tile, *kern, text])
+    # CogVideoX-2B configuration of the reference: every 7th query row, all keys
+    canvas, tile, kern, text = (13, 30, 45), (13, 3, 3), (1, 9, 9), 226
+    mod = ns["generate_sta_mask"](canvas, kern, tile, text)
+    S = text + 13 * 30 * 45
+    rows = torch.arange(0, S, 7)
+    out["full_rows"] = rows.numpy().astype(np.int32)
+    out["full_mask"] = np.packbits(mod(0, 0, rows[:, None], torch.arange(S)[None, :]).numpy())
+    # preprocess order: the token index found at each position after the reordering
+    obj = ns["SildingTileAttention"].__new__(ns["SildingTileAttention"])
+    obj.config = {"kernel_size": kern, "tile_size": tile, "img_size": canvas, "text_length": text}
+    idx = torch.arange(S, dtype=torch.float64).view(1, 1, S, 1).repeat(1, 1, 1, 1)
+    q, _, _ = obj.preprocess(idx.clone(), idx.clone(), idx.clone())
+    out["preprocess"] = q.reshape(-1).numpy().astype(np.int32)
+    return out
 
 
 def smart_layout(root: str):
@@ -162,6 +204,7 @@ def main(root: str):
         out["unmerge_proj"] = (un @ proj).reshape(-1).numpy()
         np.savez_compressed(HERE / f"{name}.npz", **out)
     np.savez_compressed(HERE / "smart_layout.npz", **smart_layout(root))
+    np.savez_compressed(HERE / "sta_layout.npz", **sta_layout(root))
     print("fixtures written to", HERE)
 
 

@@ -34,24 +34,25 @@ struct UlyssesParams {
   int32_t T, B, s, D, vec;   // vec = 16-byte vectors per D row
 };
 
-// kPack: seq -> buf; otherwise buf -> seq.
+// kPack: seq -> buf; otherwise buf -> seq.  One thread per 16-byte vector
+// (consecutive lanes cover consecutive vectors of a row: coalesced on both
+// sides), 32-bit index arithmetic.
 template <bool kPack>
 __global__ void __launch_bounds__(256) ulysses_copy_kernel(const UlyssesParams p) {
   const int j = blockIdx.y;
   const int hj = p.head_off[j + 1] - p.head_off[j];
-  const int64_t total = static_cast<int64_t>(p.s) * p.B * p.T * hj * p.vec;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int total = p.s * p.B * p.T * hj * p.vec;
+  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total) return;
-  // chunk order: (row s, b, t, h, vector)
-  int64_t r = idx;
-  const int v = static_cast<int>(r % p.vec);
-  r /= p.vec;
-  const int h = static_cast<int>(r % hj);
-  r /= hj;
-  const int t = static_cast<int>(r % p.T);
-  r /= p.T;
-  const int b = static_cast<int>(r % p.B);
-  const int s = static_cast<int>(r / p.B);
+  // chunk order: (s, b, t, h, vector)
+  const int v = idx % p.vec;
+  const int r = idx / p.vec;
+  const int h = r % hj;
+  const int q1 = r / hj;
+  const int t = q1 % p.T;
+  const int q2 = q1 / p.T;
+  const int b = q2 % p.B;
+  const int s = q2 / p.B;
   const int64_t elem_bytes = 16LL * p.vec / p.D;  // vec = D * element size / 16
   uint4* bufv = reinterpret_cast<uint4*>(static_cast<char*>(p.buf) + p.chunk_off[j] * elem_bytes) + idx;
   uint4* seqv = reinterpret_cast<uint4*>(static_cast<char*>(p.seq[t]) +
@@ -111,8 +112,9 @@ int32_t ulysses_launch(bool pack, void* const* seq, int32_t T, int32_t dtype, in
   if (s == 0) return SAF_OK;
   int32_t rc;
   if ((rc = bind_device_of(buf)) != SAF_OK) return rc;
-  const int64_t most = s * B * T * static_cast<int64_t>(hmax) * p.vec;
+  const int64_t most = s * B * T * static_cast<int64_t>(hmax) * p.vec;  // vectors of the largest chunk
   if (most == 0) return SAF_OK;
+  if (most >= (int64_t(1) << 31)) return SAF_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>((most + 255) / 256), static_cast<unsigned>(P));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (pack)

@@ -25,6 +25,9 @@
 //      line the exact winner is among the 8, otherwise the row is re-scanned
 //      exactly over all dst;
 //   3. a stable radix sort of node_max (descending) orders the src rows.
+#include <algorithm>
+#include <cub/block/block_exchange.cuh>
+#include <cub/block/block_radix_sort.cuh>
 #include <cub/device/device_segmented_radix_sort.cuh>
 
 #include <cuda_bf16.h>
@@ -469,6 +472,99 @@ __global__ void __launch_bounds__(256) tome_exact_kernel(const ExactParams e) {
 }
 
 // ---------------------------------------------------------------------------
+// Per-segment stable radix sorts with one CTA per batch row, the whole
+// segment on chip (segments up to kSortCap items; larger ones take the
+// device-wide segmented sort).  Items are read and written in a striped
+// arrangement (coalesced) and exchanged to/from the blocked arrangement whose
+// order defines stability.  Padding keys sort last (-inf for descending fp64,
+// all ones in the sorted bits for ascending int32) and stability keeps them
+// behind real keys of the same value.
+constexpr int kSortThreads = 512;
+constexpr int kSortCap = kSortThreads * 32;  // 16384
+
+template <typename K, bool kDesc, int kItems>
+__global__ void __launch_bounds__(kSortThreads) tome_block_sort_kernel(const K* __restrict__ keys,
+                                                                       const int32_t* __restrict__ vals,
+                                                                       K* __restrict__ keys_out,
+                                                                       int32_t* __restrict__ vals_out, int n,
+                                                                       int end_bit) {
+  using Sort = cub::BlockRadixSort<K, kSortThreads, kItems, int32_t>;
+  using ExK = cub::BlockExchange<K, kSortThreads, kItems>;
+  using ExV = cub::BlockExchange<int32_t, kSortThreads, kItems>;
+  union Smem {
+    typename Sort::TempStorage sort;
+    typename ExK::TempStorage exk;
+    typename ExV::TempStorage exv;
+  };
+  extern __shared__ __align__(16) uint8_t sort_smem[];
+  Smem& sm = *reinterpret_cast<Smem*>(sort_smem);
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * n;
+  const int tid = threadIdx.x;
+  K k[kItems];
+  int32_t v[kItems];
+  const K pad = kDesc ? static_cast<K>(-INFINITY) : static_cast<K>(0x7fffffff);
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    const int idx = i * kSortThreads + tid;
+    k[i] = idx < n ? keys[base + idx] : pad;
+  }
+  ExK(sm.exk).StripedToBlocked(k);
+  __syncthreads();
+  if (vals) {
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int idx = i * kSortThreads + tid;
+      v[i] = idx < n ? vals[base + idx] : 0x7fffffff;
+    }
+    ExV(sm.exv).StripedToBlocked(v);
+    __syncthreads();
+  } else {
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) v[i] = tid * kItems + i;
+  }
+  if constexpr (kDesc)
+    Sort(sm.sort).SortDescendingBlockedToStriped(k, v, 0, end_bit);
+  else
+    Sort(sm.sort).SortBlockedToStriped(k, v, 0, end_bit);
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    const int idx = i * kSortThreads + tid;
+    if (idx < n) {
+      vals_out[base + idx] = v[i];
+      if (keys_out) keys_out[base + idx] = k[i];
+    }
+  }
+}
+
+template <typename K, bool kDesc, int kItems>
+cudaError_t block_sort_items(const K* keys, const int32_t* vals, K* keys_out, int32_t* vals_out, int B, int n,
+                             int end_bit, cudaStream_t st) {
+  constexpr int smem = static_cast<int>(
+      std::max({sizeof(typename cub::BlockRadixSort<K, kSortThreads, kItems, int32_t>::TempStorage),
+                sizeof(typename cub::BlockExchange<K, kSortThreads, kItems>::TempStorage),
+                sizeof(typename cub::BlockExchange<int32_t, kSortThreads, kItems>::TempStorage)}));
+  cudaError_t e = cudaFuncSetAttribute(tome_block_sort_kernel<K, kDesc, kItems>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  tome_block_sort_kernel<K, kDesc, kItems><<<B, kSortThreads, smem, st>>>(keys, vals, keys_out, vals_out, n,
+                                                                          end_bit);
+  return cudaGetLastError();
+}
+
+// Sorts B segments of n items each (n <= kSortCap) with the smallest
+// per-thread item count that holds a segment.
+template <typename K, bool kDesc>
+cudaError_t block_sort(const K* keys, const int32_t* vals, K* keys_out, int32_t* vals_out, int B, int n,
+                       int end_bit, cudaStream_t st) {
+  if (n <= kSortThreads * 8) return block_sort_items<K, kDesc, 8>(keys, vals, keys_out, vals_out, B, n, end_bit, st);
+  if (n <= kSortThreads * 16)
+    return block_sort_items<K, kDesc, 16>(keys, vals, keys_out, vals_out, B, n, end_bit, st);
+  if (n <= kSortThreads * 24)
+    return block_sort_items<K, kDesc, 24>(keys, vals, keys_out, vals_out, B, n, end_bit, st);
+  return block_sort_items<K, kDesc, 32>(keys, vals, keys_out, vals_out, B, n, end_bit, st);
+}
+
+// ---------------------------------------------------------------------------
 // plan finalisation
 struct FinalParams {
   int B, Ns, Nd, N, r;
@@ -869,10 +965,14 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   tome_offsets_kernel<<<static_cast<unsigned>((B + 256) / 256), 256, 0, st>>>(static_cast<int>(B), static_cast<int>(Ns), seg1);
   tome_iota_kernel<<<dim3(static_cast<unsigned>((Ns + 255) / 256), static_cast<unsigned>(B)), 256, 0, st>>>(
       static_cast<int>(B), static_cast<int>(Ns), vals_in);
-  size_t tb = lay.cub_bytes;
-  SAF_CUDA_TRY(cub::DeviceSegmentedRadixSort::SortPairsDescending(
-      ws + lay.off_cub, tb, nmax, keys_out, vals_in, order, static_cast<int>(B * Ns),
-      static_cast<int>(B), seg1, seg1 + 1, 0, 64, st));
+  if (Ns <= kSortCap) {
+    SAF_CUDA_TRY((block_sort<double, true>(nmax, nullptr, nullptr, order, static_cast<int>(B), static_cast<int>(Ns), 64, st)));
+  } else {
+    size_t tb = lay.cub_bytes;
+    SAF_CUDA_TRY(cub::DeviceSegmentedRadixSort::SortPairsDescending(
+        ws + lay.off_cub, tb, nmax, keys_out, vals_in, order, static_cast<int>(B * Ns),
+        static_cast<int>(B), seg1, seg1 + 1, 0, 64, st));
+  }
 
   // 5. plan: src / dst / unm indices, token map, dst -> src lists, counters
   int32_t* dkey = reinterpret_cast<int32_t*>(ws + lay.off_dkey);
@@ -885,10 +985,18 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   SAF_CUDA_TRY(cudaGetLastError());
   if (rr > 0) {
     tome_offsets_kernel<<<static_cast<unsigned>((B + 256) / 256), 256, 0, st>>>(static_cast<int>(B), static_cast<int>(rr), seg2);
-    size_t tb2 = lay.cub_bytes;
-    SAF_CUDA_TRY(cub::DeviceSegmentedRadixSort::SortPairs(
-        ws + lay.off_cub, tb2, dkey, dkey_out, reinterpret_cast<int32_t*>(ws + lay.off_dval_out),
-        plan->dst_src, static_cast<int>(B * rr), static_cast<int>(B), seg2, seg2 + 1, 0, 32, st));
+    int dst_bits = 1;  // dst keys lie in [0, Nd)
+    while ((int64_t(1) << dst_bits) < Nd) ++dst_bits;
+    if (rr <= kSortCap) {
+      SAF_CUDA_TRY((block_sort<int32_t, false>(dkey, reinterpret_cast<int32_t*>(ws + lay.off_dval_out),
+                                               dkey_out, plan->dst_src, static_cast<int>(B), static_cast<int>(rr),
+                                               dst_bits, st)));
+    } else {
+      size_t tb2 = lay.cub_bytes;
+      SAF_CUDA_TRY(cub::DeviceSegmentedRadixSort::SortPairs(
+          ws + lay.off_cub, tb2, dkey, dkey_out, reinterpret_cast<int32_t*>(ws + lay.off_dval_out),
+          plan->dst_src, static_cast<int>(B * rr), static_cast<int>(B), seg2, seg2 + 1, 0, dst_bits, st));
+    }
   }
   tome_dstptr_kernel<<<dim3(static_cast<unsigned>((Nd + 1 + 255) / 256), static_cast<unsigned>(B)), 256, 0, st>>>(
       static_cast<int>(B), static_cast<int>(Nd), static_cast<int>(rr), dkey_out, plan->dst_ptr,

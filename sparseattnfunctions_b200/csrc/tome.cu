@@ -95,6 +95,21 @@ __device__ __forceinline__ void cand_insert(float (&v)[kCand], int (&ix)[kCand],
   }
 }
 
+// sc[e] for a runtime e in [0, 32): a 5-level select tree on the bits of e
+// (no dynamic register indexing).
+__device__ __forceinline__ float pick32(const float (&sc)[32], int e) {
+  float l1[16], l2[8], l3[4], l4[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) l1[i] = (e & 1) ? sc[2 * i + 1] : sc[2 * i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) l2[i] = (e & 2) ? l1[2 * i + 1] : l1[2 * i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) l3[i] = (e & 4) ? l2[2 * i + 1] : l2[2 * i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) l4[i] = (e & 8) ? l3[2 * i + 1] : l3[2 * i];
+  return (e & 16) ? l4[1] : l4[0];
+}
+
 // grid (ceil(Ns/128), B).  One CTA per SM (TMEM: two 256-column accumulators).
 template <bool kBF16, bool kRes>
 __global__ void __launch_bounds__(kScoreThreads, 1)
@@ -247,6 +262,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       cand_insert(cv, ci, sv, j);
     };
     bool ok = true;
+    float4 rv_next[8];
+    if (chalf * (kTN / 2) + 32 <= p.Nd) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rv_next[i] = __ldg(reinterpret_cast<const float4*>(rinv + chalf * (kTN / 2)) + i);
+    }
     for (int nt = 0; nt < n_tiles; ++nt) {
       const int buf = nt & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(bar_acc_full(buf), (nt >> 1) & 1, abort_flag,
@@ -258,6 +278,19 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       const int col0 = nt * kTN + chalf * (kTN / 2);
 #pragma unroll 1
       for (int c = 0; c < kTN / 2 / 32; ++c) {
+        const int jc = col0 + c * 32;
+        // this chunk's 1/|b| (prefetched one chunk ahead); the next chunk's
+        // loads are issued before this chunk's TMEM load
+        float4 rv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rv[i] = rv_next[i];
+        {
+          const int jn = c + 1 < kTN / 2 / 32 ? jc + 32 : (nt + 1) * kTN + chalf * (kTN / 2);
+          if (jn + 32 <= p.Nd) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) rv_next[i] = __ldg(reinterpret_cast<const float4*>(rinv + jn) + i);
+          }
+        }
         uint32_t r[32];
         tmem_ld32(tmem + lane_addr + buf * kTN + chalf * (kTN / 2) + c * 32, r);
         tmem_wait_ld(r);
@@ -265,16 +298,15 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           tc_fence_before();
           mbar_arrive(bar_acc_empty(buf));
         }
-        const int jc = col0 + c * 32;
-        // scores of the chunk (1/|b| from vector loads every lane of the warp
-        // shares); columns past Nd score -inf
+        // scores of the chunk (1/|b| shared by every lane of the warp);
+        // columns past Nd score -inf
         float sc[32];
         if (jc + 32 <= p.Nd) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
-            const float4 rv = __ldg(reinterpret_cast<const float4*>(rinv + jc + e));
-            const f2 a = mul2(mk2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), mk2(rv.x, rv.y));
-            const f2 b2 = mul2(mk2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])), mk2(rv.z, rv.w));
+            const float4 q = rv[e / 4];
+            const f2 a = mul2(mk2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), mk2(q.x, q.y));
+            const f2 b2 = mul2(mk2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])), mk2(q.z, q.w));
             sc[e] = lo2(a);
             sc[e + 1] = hi2(a);
             sc[e + 2] = lo2(b2);
@@ -285,28 +317,32 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           for (int e = 0; e < 32; ++e)
             sc[e] = jc + e < p.Nd ? __uint_as_float(r[e]) * __ldg(rinv + jc + e) : -INFINITY;
         }
-        float mx = fmax3(sc[0], sc[1], sc[2]);
+        float m4[4];
 #pragma unroll
-        for (int e = 3; e < 31; e += 2) mx = fmax3(mx, sc[e], sc[e + 1]);
-        mx = fmaxf(mx, sc[31]);
+        for (int i = 0; i < 4; ++i) m4[i] = fmax3(sc[8 * i], sc[8 * i + 1], sc[8 * i + 2]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], sc[8 * i + 3], sc[8 * i + 4]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], sc[8 * i + 5], sc[8 * i + 6]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m4[i] = fmaxf(m4[i], sc[8 * i + 7]);
+        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         // most chunks hold nothing within tau of the running maximum
         if (mx >= run_max - tau) {
           run_max = fmaxf(run_max, mx);
           const float thr = run_max - tau;
-          int cnt = 0, first = 0;
+          uint32_t mask = 0;
 #pragma unroll
-          for (int e = 31; e >= 0; --e) {
-            if (sc[e] >= thr) {
-              ++cnt;
-              first = e;
-            }
-          }
-          if (cnt == 1) {
-            add(mx, jc + first, thr);  // the chunk maximum, usually alone
+          for (int e = 0; e < 32; ++e) mask |= (sc[e] >= thr ? 1u : 0u) << e;
+          if ((mask & (mask - 1)) == 0) {
+            add(mx, jc + __ffs(mask) - 1, thr);  // the chunk maximum, usually alone
           } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (sc[e] >= thr) add(sc[e], jc + e, thr);
+            // several columns within tau: in ascending column order
+            while (mask) {
+              const int e = __ffs(mask) - 1;
+              mask &= mask - 1;
+              add(pick32(sc, e), jc + e, thr);
+            }
           }
         }
       }

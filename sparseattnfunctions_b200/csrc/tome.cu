@@ -331,9 +331,20 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         if (mx >= run_max - tau) {
           run_max = fmaxf(run_max, mx);
           const float thr = run_max - tau;
-          uint32_t mask = 0;
+          // bit e = (sc[e] >= thr): the sign bits of sc - thr, gathered by
+          // funnel shifts in four independent chains.  The sign is exact
+          // (a difference of two floats rounds to zero only when it is zero),
+          // and -thr + 0 is never -0, so sc = -0 against thr = 0 gives +0.
+          uint32_t nb[4] = {0u, 0u, 0u, 0u};
+          const float nthr = -thr + 0.0f;
+          const f2 thr2 = mk2(nthr, nthr);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mask |= (sc[e] >= thr ? 1u : 0u) << e;
+          for (int e = 30; e >= 0; e -= 2) {
+            const f2 d = add2(mk2(sc[e], sc[e + 1]), thr2);
+            const int g = (e >> 3) & 3;
+            nb[g] = __funnelshift_l(__float_as_uint(lo2(d)), __funnelshift_l(__float_as_uint(hi2(d)), nb[g], 1), 1);
+          }
+          uint32_t mask = ~(nb[0] | (nb[1] << 8) | (nb[2] << 16) | (nb[3] << 24));
           if ((mask & (mask - 1)) == 0) {
             add(mx, jc + __ffs(mask) - 1, thr);  // the chunk maximum, usually alone
           } else {

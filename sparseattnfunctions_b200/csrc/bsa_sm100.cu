@@ -64,6 +64,7 @@ struct BsaParams {
   const float* kv_bias;    // nullable
   int64_t bias_stride;     // per head, elements
   float scale_log2;        // sm_scale * log2(e)
+  float inv_scale;         // 1 / sm_scale
   void* o;
   int64_t o_sb, o_sh, o_ss;  // element strides
   unsigned int* status;
@@ -180,18 +181,25 @@ __device__ __forceinline__ f2 exp2_poly2(f2 x) {
 #endif
 __host__ __device__ constexpr bool exp2_on_fma(int e) { return (SAF_EXP2_FMA_MASK >> e) & 1u; }
 
-template <int BN>
+// With a key bias, S = Q K^T + 1 b'^T: one more K = 16 MMA per tile whose A
+// is a ones column (row m: [1, 0, ..., 0]) and whose B rows carry
+// b'_j = bias_j / sm_scale in column 0 (16-bit, 32-byte swizzled tiles written
+// by the producer warp).  Scaling S by sm_scale * log2(e) then adds
+// bias_j * log2(e) to every logit, with no per-element work in the softmax.
+template <int BN, bool kBias>
 struct Layout {
   static constexpr int kQBytes = kBM * kD * 2;  // 16 KB
   static constexpr int kKVBytes = BN * kD * 2;  // 16 / 8 KB
+  static constexpr int kBiasTile = BN * 32;     // BN rows x 16 16-bit values
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + kKS * kKVBytes;
-  static constexpr int kOffBias = kOffV + kVS * kKVBytes;
-  static constexpr int kOffBar = kOffBias + kVS * BN * 4;
+  static constexpr int kOffBias = kOffV + kVS * kKVBytes;          // [kVS] bias tiles
+  static constexpr int kOffOnes = kOffBias + (kBias ? kVS * kBiasTile : 0);  // ones column
+  static constexpr int kOffBar = kOffOnes + (kBias ? kBM * 32 : 0);
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain
-  static constexpr int kNumBars = 1 + 2 * kKS + 3 * kVS + 5;
+  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain, b_empty[VS]
+  static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
@@ -202,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     bsa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const BsaParams p) {
-  using L = Layout<BN>;
+  using L = Layout<BN, kBias>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -232,7 +240,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t sQ = smem_u32(smem + L::kOffQ);
   const uint32_t sK0 = smem_u32(smem + L::kOffK);
   const uint32_t sV0 = smem_u32(smem + L::kOffV);
-  float* sBias = reinterpret_cast<float*>(smem + L::kOffBias);
+  const uint32_t sBias0 = smem_u32(smem + L::kOffBias);
+  const uint32_t sOnes = smem_u32(smem + L::kOffOnes);
   const uint32_t bar0 = smem_u32(smem + L::kOffBar);
   const uint32_t bar_q = bar0;
   auto bar_k_full = [&](int s) { return bar0 + 8u * (1 + s); };
@@ -240,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto bar_v_full = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + s); };
   auto bar_v_empty = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + kVS + s); };
   auto bar_b_full = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + 2 * kVS + s); };
+  auto bar_b_empty = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + 3 * kVS + 5 + s); };
   const uint32_t bar_s_full = bar0 + 8u * (1 + 2 * kKS + 3 * kVS);
   const uint32_t bar_s_empty = bar_s_full + 8;
   const uint32_t bar_p_full = bar_s_full + 16;
@@ -258,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar_v_full(s), 1);
       mbar_init(bar_v_empty(s), 1);
       mbar_init(bar_b_full(s), 32);
+      mbar_init(bar_b_empty(s), 1);
     }
     mbar_init(bar_s_full, 1);
     mbar_init(bar_s_empty, 128);  // the softmax threads
@@ -269,6 +280,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+  }
+  if constexpr (kBias) {
+    // the ones column: 128 rows x 32 bytes, 32-byte swizzle (the 16-byte
+    // half holding element 0 of row m is (m >> 2) & 1)
+    const int m = threadIdx.x >> 1, half = threadIdx.x & 1;
+    const uint32_t one = kBF16 ? 0x3F80u : 0x3C00u;
+    const uint32_t w0 = half == ((m >> 2) & 1) ? one : 0u;
+    st_shared_v4(sOnes + m * 32 + half * 16, w0, 0u, 0u, 0u);
+    fence_proxy_async_smem();
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -296,11 +316,40 @@ __global__ void __launch_bounds__(kThreads, 2)
     while (it.next(col, rm)) {
       const int sk = nk % kKS, sv = nv % kVS;
       const uint32_t pk = (nk / kKS) & 1, pv = (nv / kVS) & 1;
+      // this block's key biases (loads in flight across the K-stage wait)
+      float bvals[BN / 32];
+      if constexpr (kBias) {
+        const float* src = p.kv_bias + static_cast<int64_t>(g) * p.bias_stride;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) {
+          const int kv = col * BN + lane + 32 * i;
+          bvals[i] = kv < p.Sk ? src[kv] : 0.f;
+        }
+      }
       bool ok = mbar_wait(bar_k_empty(sk), pk ^ 1, abort_flag, p.status, p.budget_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
       if (lane == 0) {
         mbar_arrive_expect_tx(bar_k_full(sk), L::kKVBytes);
         tma_load_4d(sK0 + sk * L::kKVBytes, &tm_k, bar_k_full(sk), 0, col * BN, h, b);
+      }
+      if constexpr (kBias) {
+        // B rows of the bias MMA of block nk (its own 2-stage ring, freed by
+        // that MMA's commit): key row c holds bias / sm_scale in element 0
+        const int sb = nk % kVS;
+        ok = mbar_wait(bar_b_empty(sb), ((nk / kVS) & 1) ^ 1, abort_flag, p.status, p.budget_ns);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const uint32_t dst = sBias0 + sb * L::kBiasTile;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) {
+          const int c = lane + 32 * i;
+          const float bv = bvals[i] * p.inv_scale;
+          const uint32_t bits = kBF16 ? pack_bf16x2(bv, 0.f) : pack_f16x2(bv, 0.f);  // [bv, 0]
+          const int hv = (c >> 2) & 1;
+          st_shared_v4(dst + c * 32 + hv * 16, bits, 0u, 0u, 0u);
+          st_shared_v4(dst + c * 32 + (hv ^ 1) * 16, 0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bar_b_full(sb));
       }
       ++nk;
       ok = mbar_wait(bar_v_empty(sv), pv ^ 1, abort_flag, p.status, p.budget_ns);
@@ -310,15 +359,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_4d(sV0 + sv * L::kKVBytes, &tm_v, bar_v_full(sv), 0, col * BN, h, b);
       }
       ++nv;
-      if constexpr (kBias) {
-        const float* src = p.kv_bias + static_cast<int64_t>(g) * p.bias_stride;
-        float* dst = sBias + sv * BN;
-        for (int c = lane; c < BN; c += 32) {
-          const int kv = col * BN + c;
-          dst[c] = kv < p.Sk ? src[kv] * kLog2e : 0.f;
-        }
-        mbar_arrive(bar_b_full(sv));
-      }
     }
     // Drain: wait for the last load issued into every stage (and so for all
     // earlier ones).  Immediate on the normal path, where the consumers have
@@ -386,8 +426,14 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint64_t bdesc = sdesc_sw128(kbase + kk * 32, 16, 1024);
           tc_mma_ss(tS, adesc, bdesc, kIdescQK, kk > 0 ? 1u : 0u);
         }
+        if constexpr (kBias) {
+          const int sb = j % kVS;
+          if (!mbar_wait(bar_b_full(sb), (j / kVS) & 1, abort_flag, p.status, p.budget_ns)) break;
+          tc_mma_ss(tS, sdesc_sw32(sOnes, 256), sdesc_sw32(sBias0 + sb * L::kBiasTile, 256), kIdescQK, 1u);
+        }
         tc_commit(bar_s_full);
         tc_commit(bar_k_empty(sk));
+        if constexpr (kBias) tc_commit(bar_b_empty(j % kVS));
         if (j > 0 && !issue_pv(j - 1)) break;
         ++j;
       }
@@ -458,27 +504,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool fast = live && valid >= BN;
       if constexpr (kRanges)
         fast = fast && ((c0 >= lo0 && c0 + BN <= hi0) || (c0 >= lo1 && c0 + BN <= hi1));
+      // (a key bias is already in S: see Layout)
       float t[BN];
-      if constexpr (kBias) {
-        const int sv = j % kVS;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_b_full(sv), (j / kVS) & 1, abort_flag,
-                                                p.status, p.budget_ns))) {
-          ok = false;
-          break;
-        }
-        const float* bb = sBias + sv * BN;
 #pragma unroll
-        for (int e = 0; e < BN; e += 2) {
-          const float2 bv = *reinterpret_cast<const float2*>(bb + e);
-          const f2 x = fma2(mk2(__uint_as_float(r[e / 32][e % 32]), __uint_as_float(r[e / 32][e % 32 + 1])),
-                            sl2x2, mk2(bv.x, bv.y));
-          t[e] = lo2(x);
-          t[e + 1] = hi2(x);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < BN; ++e) t[e] = __uint_as_float(r[e / 32][e % 32]);
-      }
+      for (int e = 0; e < BN; ++e) t[e] = __uint_as_float(r[e / 32][e % 32]);
       if (!fast) {
         if constexpr (kRanges) {
           const int a0 = lo0 - c0, b0 = hi0 - c0, a1 = lo1 - c0, b1 = hi1 - c0;
@@ -530,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (with_max)
               acc[e & 3] = fmax3(acc[e & 3], t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
             f2 x = mk2(t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
-            x = kBias ? add2(x, negm2) : fma2(x, sl2x2, negm2);
+            x = fma2(x, sl2x2, negm2);
             float e0, e1;
             if (exp2_on_fma(e)) {
               const f2 y = exp2_poly2(x);
@@ -571,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int i = 0; i < BN / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
         mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
       }
-      if constexpr (!kBias) mx *= sl2;
+      mx *= sl2;
       const bool upd = mx > m_run + kRescaleThreshold;
       const float m_new = upd ? mx : m_run;
       const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
@@ -677,7 +706,7 @@ template <int BN, bool kBias, bool kBF16, bool kRanges>
 int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                        const BsaParams& p, int n_tiles, cudaStream_t stream) {
   auto kern = bsa_fwd_sm100_kernel<BN, kBias, kBF16, kRanges>;
-  const int smem = Layout<BN>::kDynSmem;
+  const int smem = Layout<BN, kBias>::kDynSmem;
   SAF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid(n_tiles, p.B * p.H);
   kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
@@ -715,6 +744,7 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   p.kv_bias = kv_bias;
   p.bias_stride = bias_stride;
   p.scale_log2 = sm_scale * kLog2e;
+  p.inv_scale = static_cast<float>(1.0 / static_cast<double>(sm_scale));
   p.o = o->data;
   p.o_sb = o->stride_b;
   p.o_sh = o->stride_h;

@@ -310,6 +310,23 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// Shared-memory matrix descriptor, K-major, 32-byte swizzle (one 16-element
+// K slice of 16-bit values per 32-byte row; 8-row atoms of 256 bytes).
+__device__ __forceinline__ uint64_t sdesc_sw32(uint32_t saddr, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;  // leading byte offset: unused for K-major swizzled
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(6) << 61;
+  return d;
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation:
 // [4,6) D format (1 = f32), [7,10) A format, [10,13) B format (0 = f16,
 // 1 = bf16), bit 15 A MN-major, bit 16 B MN-major, [17,23) N >> 3,

@@ -347,13 +347,18 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           uint32_t mask = ~(nb[0] | (nb[1] << 8) | (nb[2] << 16) | (nb[3] << 24));
           if ((mask & (mask - 1)) == 0) {
             add(mx, jc + __ffs(mask) - 1, thr);  // the chunk maximum, usually alone
-          } else {
-            // several columns within tau: in ascending column order
+          } else if (__popc(mask) <= 4) {
+            // a few columns within tau: in ascending column order
             while (mask) {
               const int e = __ffs(mask) - 1;
               mask &= mask - 1;
               add(pick32(sc, e), jc + e, thr);
             }
+          } else {
+            // many (near-duplicate dst rows): every column, predicated
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if ((mask >> e) & 1u) add(sc[e], jc + e, thr);
           }
         }
       }

@@ -669,7 +669,18 @@ def run_reference(args, world, rank):
     }
 
 
+def _json_out():
+    """The real stdout, kept for the one JSON line; file descriptor 1 is
+    pointed at stderr so that anything native code prints there (NCCL's
+    version banner, library messages) cannot mix into the result."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def main():
+    out = _json_out()
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
@@ -694,7 +705,7 @@ def main():
     if args.impl == "reference":
         line = run_reference(args, world, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=out, flush=True)
         return
 
     line, qkv_cpu, csr, cfg = run_saf(args, world, rank, local)
@@ -707,7 +718,7 @@ def main():
                                 "sample": f"{heads} of 60 (b,h) heads of config 2 in {secs:.1f} s: "
                                           "query-chunked (2048) bf16 masked SDPA, same block mask"}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=out, flush=True)
     if world > 1:
         import torch.distributed as dist
 

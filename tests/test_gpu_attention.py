@@ -115,6 +115,28 @@ def test_kv_bias(cuda_device, bn):
     _run(cuda_device, 2, 2, 777, 1111, 64, torch.bfloat16, 128, bn, 0.4, seed=11, bias=True)
 
 
+@pytest.mark.parametrize("dtype,bn", [(torch.float16, 128), (torch.float16, 64), (torch.bfloat16, 128)])
+def test_kv_bias_masking_values(cuda_device, dtype, bn):
+    """The bias enters S through the tensor cores in the input's 16-bit type:
+    -inf keys must vanish, large negative biases must act as masks, and a
+    head whose keys are all -inf in one block must still see its other
+    blocks (the bias is per head)."""
+    B, H, Sq, Sk, D = 1, 2, 600, 700, 64
+    q, k, v = _inputs(B, H, Sq, Sk, D, dtype, seed=41)
+    mask = torch.ones(B, H, math.ceil(Sq / 128), math.ceil(Sk / bn), dtype=torch.bool)
+    g = torch.Generator().manual_seed(42)
+    bias = torch.log(torch.randint(1, 14, (B * H, Sk), generator=g).float())
+    bias[:, 5:40] = float("-inf")
+    bias[:, 100:130] = -1.0e4
+    bias[1, bn:2 * bn] = float("-inf")  # a whole key block of head 1
+    csr = kernels.mask_to_csr(mask.to(cuda_device), 128, bn)
+    out = kernels.bsa_fwd(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), csr, 1 / 8,
+                          kv_bias=bias.to(cuda_device))
+    torch.cuda.synchronize()
+    ref = oatt.block_sparse_attention(q, k, v, mask, 1 / 8, 128, bn, kv_bias=bias)
+    _compare(out, ref, TOL[dtype])
+
+
 def test_dense_long_rows(cuda_device):
     """Every block live (the dense path of MergeAttention) at S = 4000."""
     _run(cuda_device, 1, 2, 4000, 4000, 64, torch.bfloat16, 128, 128, 1.01, seed=3)

@@ -188,16 +188,43 @@ __global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
 
   const double* kb = a.kbar + static_cast<int64_t>(g) * a.nbk * a.D;
   const double* qb = a.qbar + static_cast<int64_t>(g) * a.nbq * a.D;
+  // staging: every thread issues its loads 8 at a time before storing them
+  // (a few memory round trips per chunk instead of one per element)
+  constexpr int kKLoads = (32 * M * kDChunk + 255) / 256;
+  constexpr int kQLoads = (kRowsPerCta * kDChunk + 255) / 256;
   for (int d0 = 0; d0 < a.D; d0 += kDChunk) {
     __syncthreads();
-    for (int idx = threadIdx.x; idx < a.nbk * kDChunk; idx += blockDim.x) {
-      const int j = idx / kDChunk, d = idx % kDChunk;
-      ks[j * (kDChunk + 1) + d] = kb[static_cast<int64_t>(j) * a.D + d0 + d];
+#pragma unroll 1
+    for (int u0 = 0; u0 < kKLoads; u0 += 8) {
+      double kt[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = threadIdx.x + 256 * (u0 + u);
+        const int j = idx / kDChunk, d = idx % kDChunk;
+        kt[u] = (u0 + u < kKLoads && j < a.nbk) ? kb[static_cast<int64_t>(j) * a.D + d0 + d] : 0.0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = threadIdx.x + 256 * (u0 + u);
+        const int j = idx / kDChunk, d = idx % kDChunk;
+        if (u0 + u < kKLoads && j < a.nbk) ks[j * (kDChunk + 1) + d] = kt[u];
+      }
+      asm volatile("" ::: "memory");  // keep the next group's loads after these stores
     }
-    for (int idx = threadIdx.x; idx < kRowsPerCta * kDChunk; idx += blockDim.x) {
-      const int r = idx / kDChunk, d = idx % kDChunk;
-      const int rr = blockIdx.y * kRowsPerCta + r;
-      qs[r * (kDChunk + 1) + d] = rr < a.nbq ? qb[static_cast<int64_t>(rr) * a.D + d0 + d] : 0.0;
+    {
+      double qt[kQLoads];
+#pragma unroll
+      for (int u = 0; u < kQLoads; ++u) {
+        const int idx = threadIdx.x + 256 * u;
+        const int r = idx / kDChunk, d = idx % kDChunk;
+        const int rr = blockIdx.y * kRowsPerCta + r;
+        qt[u] = rr < a.nbq ? qb[static_cast<int64_t>(rr) * a.D + d0 + d] : 0.0;
+      }
+#pragma unroll
+      for (int u = 0; u < kQLoads; ++u) {
+        const int idx = threadIdx.x + 256 * u;
+        qs[(idx / kDChunk) * (kDChunk + 1) + idx % kDChunk] = qt[u];
+      }
     }
     __syncthreads();
     const double* qr = qs + warp * kRowsPerWarp * (kDChunk + 1);

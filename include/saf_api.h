@@ -186,6 +186,26 @@ int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k, const saf
                            const float* kv_bias, int64_t kv_bias_stride_bh, float sm_scale,
                            int32_t lead_rows, const int32_t* row_ranges, void* stream);
 
+/* Attention with a pooled attention map.  Runs the block-sparse attention
+ * (16-bit inputs, no key bias) and writes pool_out [B*H, nbp, nbk] fp32,
+ * nbp = ceil(Sq / pool_block), nbk = ceil(Sk / block_n):
+ *   pool_out[g, i, j] = max over query rows r of block i of
+ *                       exp2(R[r, j] - lse_r),
+ * R[r, j] = row r's largest logit in key block j (log2 units, sm_scale
+ * folded in; -inf for blocks the row does not visit), lse_r = the row's
+ * log2-sum-exp; then every row of pool_out is divided by its sum.
+ * workspace: caller-allocated, at least saf_bsa_pool_workspace_bytes(B*H,
+ * Sq, nbk) bytes (R and lse in fp32).  fp32 inputs: SAF_ERR_UNSUPPORTED.
+ * Replaces: attn_with_pooling / _attention_pooling.forward and _attn_fwd
+ * (special_attentions/utils/attn_pooling_kernel.py:25-97,106-264; the
+ * non-causal case, whose query and key blocks are both block_size). */
+int64_t saf_bsa_pool_workspace_bytes(int64_t BH, int64_t Sq, int32_t nbk);
+int32_t saf_bsa_fwd_pool(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                         const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
+                         int64_t col_capacity, int32_t block_m, int32_t block_n, float sm_scale,
+                         int32_t lead_rows, int32_t pool_block, void* workspace,
+                         int64_t workspace_bytes, float* pool_out, void* stream);
+
 /* ---- (3) ToMe token merging -----------------------------------------
  * Output buffers of a bipartite matching.  Positions refer to the src list
  * a_idx (length Ns) and the dst list b_idx (length Nd) of video tokens.

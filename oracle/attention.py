@@ -63,6 +63,44 @@ def block_sparse_attention(q, k, v, block_mask, sm_scale: float, block_m: int, b
     return out
 
 
+def attention_with_pooling(q, k, v, sm_scale: float, block_size: int, block_mask=None):
+    """fp64 attention with the pooled attention map of
+    special_attentions/utils/attn_pooling_kernel.py (non-causal path).
+
+    Per query row r and key block j: R[r, j] = max logit of r in block j
+    (:43-47), p[r, j] = exp(R[r, j] - m_r) / l_r with the row's softmax max
+    and sum (:81-97, written there in log2 units), pool[i, j] = max of p over
+    the rows of query block i (block_size rows), then every pool row divided
+    by its sum (:254-255).  ``block_mask`` (optional, [B,H,nbq,nbk] over
+    block_size x block_size blocks) restricts the keys a row sees; blocks it
+    does not see contribute 0.  Returns (out [B,H,Sq,D], pool [B,H,nbq,nbk]).
+    """
+    q, k, v = to_f64(q), to_f64(k), to_f64(v)
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    nbq, nbk = math.ceil(Sq / block_size), math.ceil(Sk / block_size)
+    mask = np.ones((B, H, nbq, nbk), dtype=bool) if block_mask is None else np.asarray(to_f64(block_mask) != 0)
+    out = np.full((B, H, Sq, D), np.nan, dtype=np.float64)
+    pool = np.zeros((B, H, nbq, nbk), dtype=np.float64)
+    for b in range(B):
+        for h in range(H):
+            tok = np.repeat(np.repeat(mask[b, h], block_size, axis=0), block_size, axis=1)[:Sq, :Sk]
+            logits = (q[b, h] @ k[b, h].T) * sm_scale
+            logits = np.where(tok, logits, -np.inf)
+            m = logits.max(axis=1, keepdims=True)
+            e = np.exp(logits - m)
+            l = e.sum(axis=1, keepdims=True)
+            out[b, h] = (e / l) @ v[b, h]
+            pad = nbk * block_size - Sk
+            lp = np.pad(logits, ((0, 0), (0, pad)), constant_values=-np.inf)
+            rmax = lp.reshape(Sq, nbk, block_size).max(axis=2)        # R[r, j]
+            p = np.exp(rmax - m) / l                                  # 0 where R = -inf
+            for i in range(nbq):
+                pool[b, h, i] = p[i * block_size:(i + 1) * block_size].max(axis=0)
+    pool = pool / pool.sum(axis=-1, keepdims=True)
+    return out, pool
+
+
 def expand_block_mask(block_mask, Sq: int, Sk: int, block_m: int, block_n: int):
     """Token-level mask from a block mask, like ``torch.kron(mask, ones)``
     cropped to ``[:Sq, :Sk]`` (block_sparse_attn_kernel.py:326-328)."""

@@ -117,6 +117,9 @@ SIGNATURES = {
                            _P]),
     "saf_bsa_fwd_ranges": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I64, _F32,
                                   _I32, _P, _P]),
+    "saf_bsa_pool_workspace_bytes": (_I64, [_I64, _I64, _I32]),
+    "saf_bsa_fwd_pool": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _F32, _I32, _I32, _P,
+                                _I64, _P, _P]),
     "saf_tome_match_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I32]),
     "saf_tome_match": (_I32, [_P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I32,
                               ctypes.POINTER(TomePlan), _P, _SZ, _P]),

@@ -16,7 +16,7 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
                       int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
-                      cudaStream_t stream);
+                      float* pool_rmax, float* pool_lse, cudaStream_t stream);
 
 namespace {
 
@@ -259,13 +259,13 @@ int32_t check_operand(const saf_tensor4* t, const saf_tensor4* ref) {
 
 using namespace saf;
 
-extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k,
-                                      const saf_tensor4* v, const saf_tensor4* o,
-                                      const int32_t* row_ptr, const int32_t* col_idx,
-                                      int64_t col_capacity, int32_t block_m, int32_t block_n,
-                                      const float* kv_bias, int64_t kv_bias_stride_bh,
-                                      float sm_scale, int32_t lead_rows, const int32_t* row_ranges,
-                                      void* stream) {
+// Validation and dispatch shared by the attention entry points; pool_rmax /
+// pool_lse (16-bit path only) receive the pooled-map statistics.
+int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                      const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
+                      int64_t col_capacity, int32_t block_m, int32_t block_n, const float* kv_bias,
+                      int64_t kv_bias_stride_bh, float sm_scale, int32_t lead_rows,
+                      const int32_t* row_ranges, float* pool_rmax, float* pool_lse, void* stream) {
   int32_t rc = check_tensor4(q);
   if (rc != SAF_OK) return rc;
   if ((rc = check_operand(k, q)) != SAF_OK) return rc;
@@ -281,6 +281,7 @@ extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k
   if (row_ranges != nullptr && kv_bias != nullptr) return SAF_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (q->dtype == SAF_F32) {
+    if (pool_rmax != nullptr || pool_lse != nullptr) return SAF_ERR_UNSUPPORTED;
     if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
     return bsa_fwd_simt(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                         kv_bias_stride_bh, sm_scale, row_ranges, st);
@@ -300,7 +301,19 @@ extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k
   const int64_t lead_tiles = (static_cast<int64_t>(lead_rows) * block_m + 127) / 128;
   return bsa_fwd_sm100(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                        kv_bias_stride_bh, sm_scale,
-                       static_cast<int>(lead_tiles < 65535 ? lead_tiles : 65535), row_ranges, st);
+                       static_cast<int>(lead_tiles < 65535 ? lead_tiles : 65535), row_ranges,
+                       pool_rmax, pool_lse, st);
+}
+
+extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k,
+                                      const saf_tensor4* v, const saf_tensor4* o,
+                                      const int32_t* row_ptr, const int32_t* col_idx,
+                                      int64_t col_capacity, int32_t block_m, int32_t block_n,
+                                      const float* kv_bias, int64_t kv_bias_stride_bh,
+                                      float sm_scale, int32_t lead_rows, const int32_t* row_ranges,
+                                      void* stream) {
+  return bsa_fwd_entry(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
+                       kv_bias_stride_bh, sm_scale, lead_rows, row_ranges, nullptr, nullptr, stream);
 }
 
 extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,

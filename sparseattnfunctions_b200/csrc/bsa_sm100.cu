@@ -73,6 +73,11 @@ struct BsaParams {
   // nullable [Sq] int4: the key columns of query row r are limited to
   // [x, y) U [z, w) (frame-band masks); shared by every head
   const int4* row_ranges;
+  // nullable pooled-map outputs (attention with pooling): per visited key
+  // block the row's maximum logit in log2 units, [B*H, nbk, Sq], and the
+  // row's log2-sum-exp, [B*H, Sq]
+  float* pool_rmax;
+  float* pool_lse;
 };
 
 // Iterates the live kv tiles of one 128-row query tile.  With 64-row mask
@@ -601,6 +606,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
       }
       mx *= sl2;
+      if (p.pool_rmax != nullptr && q0 + row < p.Sq)
+        p.pool_rmax[(static_cast<int64_t>(g) * p.nbk + col) * p.Sq + q0 + row] = mx;
       const bool upd = mx > m_run + kRescaleThreshold;
       const float m_new = upd ? mx : m_run;
       const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
@@ -646,6 +653,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (have_o) tc_fence_after();
     const int qrow = q0 + row;
     const float inv_l = 1.f / l_run;
+    if (p.pool_lse != nullptr && qrow < p.Sq)
+      p.pool_lse[static_cast<int64_t>(g) * p.Sq + qrow] = m_run + log2f(l_run);
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
                    2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
                         static_cast<int64_t>(qrow) * p.o_ss);
@@ -721,7 +730,7 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
                       int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
-                      cudaStream_t stream) {
+                      float* pool_rmax, float* pool_lse, cudaStream_t stream) {
   if (q->D != kD) return SAF_ERR_UNSUPPORTED;
   if (row_ranges != nullptr && kv_bias != nullptr) return SAF_ERR_UNSUPPORTED;
   if (!current_device_is_sm100()) return SAF_ERR_UNSUPPORTED;
@@ -753,6 +762,8 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   p.budget_ns = wait_budget_ns();
   p.lead_tiles = lead_tiles;
   p.row_ranges = reinterpret_cast<const int4*>(row_ranges);
+  p.pool_rmax = pool_rmax;
+  p.pool_lse = pool_lse;
   if (p.status == nullptr) return SAF_ERR_CUDA;
   const int n_tiles = static_cast<int>((q->S + kBM - 1) / kBM);
   const bool bf16 = q->dtype == SAF_BF16;

@@ -199,7 +199,10 @@ def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm
     """Block-sparse attention over the live blocks of ``csr``.
 
     ``kv_bias``: optional fp32 additive bias per key column, shape ``[Sk]``
-    (shared by all heads), ``[B*H, Sk]`` or ``[B, H, Sk]`` / ``[B, H, 1, Sk]``.
+    (shared by all heads), ``[B*H, Sk]`` or ``[B, H, Sk]`` / ``[B, H, 1, Sk]``;
+    with 16-bit inputs it enters the scores through the tensor cores as
+    ``bias / sm_scale`` rounded to the input type (the reference's attention
+    mask is bf16 as well).
     ``row_ranges``: optional int32 ``[Sq, 4]`` -- query row r sees only the
     keys in ``[x, y) U [z, w)`` (frame-band masks; shared by all heads; not
     combinable with ``kv_bias``).
@@ -243,6 +246,41 @@ def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm
                                             int(csr.dense_rows), rr_ptr, _stream_ptr(dev))
     _lib.check("saf_bsa_fwd", rc)
     return out
+
+
+def bsa_fwd_pool(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm_scale: float,
+                 pool_block: Optional[int] = None, out: Optional[torch.Tensor] = None):
+    """Block-sparse attention plus the pooled attention map of
+    ``attn_pooling_kernel.py``: returns ``(out, pool)`` with ``pool`` fp32
+    ``[B, H, ceil(Sq / pool_block), nbk]``, entry (i, j) the largest
+    normalised probability any query row of block i gives a key of block j
+    (0 for blocks the row does not visit), each row divided by its sum.
+    16-bit inputs; ``pool_block`` defaults to the key block size."""
+    dev = _require_cuda(q, k, v)
+    q, k, v = _d_last(q), _d_last(k), _d_last(v)
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if k.shape[:2] != (B, H) or v.shape != k.shape or k.shape[3] != D:
+        raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} do not match")
+    if (csr.B, csr.H) != (B, H) or csr.nbq != math.ceil(Sq / csr.block_m) or \
+            csr.nbk != math.ceil(Sk / csr.block_n):
+        raise ValueError("block list does not match q/k shapes")
+    pb = int(pool_block or csr.block_n)
+    nbp = math.ceil(Sq / pb)
+    if out is None:
+        out = torch.empty_like(q)
+    lib = _lib.load()
+    ws_bytes = int(lib.saf_bsa_pool_workspace_bytes(B * H, Sq, csr.nbk))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    pool = torch.empty(B, H, nbp, csr.nbk, dtype=torch.float32, device=dev)
+    tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
+    with torch.cuda.device(dev):
+        rc = lib.saf_bsa_fwd_pool(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(to),
+                                  csr.row_ptr.data_ptr(), csr.col_idx.data_ptr(), csr.col_idx.numel(),
+                                  csr.block_m, csr.block_n, float(sm_scale), int(csr.dense_rows), pb,
+                                  ws.data_ptr(), ws_bytes, pool.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_bsa_fwd_pool", rc)
+    return out, pool
 
 
 def permute_tokens(x: torch.Tensor, perm: torch.Tensor, heads: Optional[torch.Tensor] = None,

@@ -13,8 +13,13 @@ of the pooled logits, weighted by key block size) instead of the reference's
 random 8-of-64 token sample (mask_related.py:14-81); the selection rule is the
 reference's, computed on the GPU (``saf_energy_select``), and dense warm-up
 steps run the same kernel with every block live (the reference calls
-sageattention, which is not part of this path).  Sparsity records are kept
-in memory (``sparsity_records``); nothing is printed or written to files.
+sageattention, which is not part of this path).  With
+``warmup_pooling=True`` the warm-up steps run the attention with a pooled
+attention map (``utils/attn_pooling_kernel.py``) and the first sparse step of
+every layer selects its blocks from the last warm-up map of that layer (an
+exact block-level attention estimate obtained in the dense pass) instead of
+the mean-pool estimate.  Sparsity records are kept in memory
+(``sparsity_records``); nothing is printed or written to files.
 """
 from __future__ import annotations
 
@@ -53,7 +58,7 @@ def concentrated_interpolation(min_val, max_val, n_points, concentration=0.2):
 
 class BlockSparseAttention:
     def __init__(self, block_size: int = 64, layernum: int = 42, timestep: int = 50, num_samples: int = 1,
-                 warmup_epoch: int = 5, text_blocks: int = 4):
+                 warmup_epoch: int = 5, text_blocks: int = 4, warmup_pooling: bool = False):
         self.block_size = block_size
         self.sm_scale = 1 / 8
         self.layernum = layernum
@@ -70,6 +75,8 @@ class BlockSparseAttention:
         self.min_retain_ratio_list = concentrated_interpolation(0.1, 0.12, 50, concentration=0.5)
         self.energy_threshold_list = concentrated_interpolation(0.9, 0.98, 50, concentration=0.5)
         self.last_mass = None
+        self.warmup_pooling = warmup_pooling
+        self.warmup_map = [None] * layernum  # pooled map of the layer's last warm-up step
 
     def schedule(self, step: int):
         """(max_retain_ratio, min_retain_ratio, energy_threshold) of a step."""
@@ -77,16 +84,21 @@ class BlockSparseAttention:
         return (float(self.max_retain_ratio_list[i]), float(self.min_retain_ratio_list[i]),
                 float(self.energy_threshold_list[i]))
 
-    def select(self, q: torch.Tensor, k: torch.Tensor, step: int) -> kernels.BlockCSR:
+    def select(self, q: torch.Tensor, k: torch.Tensor, step: int, layer: int = 0) -> kernels.BlockCSR:
         bs = self.block_size
         Sk = k.shape[2]
-        pooled = kernels.pool_topk(q, k, block_m=bs, block_n=bs, topk=1, return_scores=True)
-        nbk = pooled.nbk
+        nbk = math.ceil(Sk / bs)
         max_r, min_r, thr = self.schedule(step)
-        mask, mass = kernels.energy_select(pooled.scores, threshold=thr, min_retain=max(1, int(nbk * min_r)),
-                                           max_retain=max(1, int(nbk * max_r)), text_blocks=self.text_blocks,
-                                           is_mass=False, scale=self.sm_scale, block_n=bs, Sk=Sk,
-                                           return_mass=True)
+        keep = dict(threshold=thr, min_retain=max(1, int(nbk * min_r)), max_retain=max(1, int(nbk * max_r)),
+                    text_blocks=self.text_blocks, return_mass=True)
+        wmap = self.warmup_map[layer] if self.warmup_pooling else None
+        if wmap is not None:
+            self.warmup_map[layer] = None
+            mask, mass = kernels.energy_select(wmap, is_mass=True, **keep)
+        else:
+            pooled = kernels.pool_topk(q, k, block_m=bs, block_n=bs, topk=1, return_scores=True)
+            mask, mass = kernels.energy_select(pooled.scores, is_mass=False, scale=self.sm_scale, block_n=bs,
+                                               Sk=Sk, **keep)
         self.last_mass = mass
         return kernels.mask_to_csr(mask, bs, bs, dense_rows=min(self.text_blocks, mask.shape[2]))
 
@@ -94,7 +106,7 @@ class BlockSparseAttention:
         self.sm_scale = 1 / q.size(-1) ** 0.5
         counter = self.counter % (self.layernum * self.timestep)
         layer, step = counter % self.layernum, counter // self.layernum
-        csr = self.select(q, k, step)
+        csr = self.select(q, k, step, layer)
         self.mask[layer] = csr
         out = kernels.bsa_fwd(q, k, v, csr, self.sm_scale)
         sparsity = 1.0 - float(csr.nnz_per_head().sum()) / (csr.B * csr.H * csr.nbq * csr.nbk)
@@ -104,17 +116,20 @@ class BlockSparseAttention:
                 {"timestep": step, "layer": layer, "sparsity": sparsity})
         return out
 
-    def dense(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    def dense(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer: int = 0) -> torch.Tensor:
         bs = self.block_size
         B, H, Sq, _ = q.shape
         nbq, nbk = math.ceil(Sq / bs), math.ceil(k.shape[2] / bs)
         csr = kernels.mask_to_csr(torch.ones(B, H, nbq, nbk, dtype=torch.bool, device=q.device), bs, bs)
+        if self.warmup_pooling:
+            out, self.warmup_map[layer] = kernels.bsa_fwd_pool(q, k, v, csr, 1 / q.size(-1) ** 0.5, pool_block=bs)
+            return out
         return kernels.bsa_fwd(q, k, v, csr, 1 / q.size(-1) ** 0.5)
 
     def __call__(self, q, k, v):
         counter = self.counter % (self.layernum * self.timestep)
         if counter // self.layernum < self.warmup_epoch:
-            out = self.dense(q, k, v)
+            out = self.dense(q, k, v, counter % self.layernum)
         else:
             out = self.forward(q, k, v)
         self.counter += 1

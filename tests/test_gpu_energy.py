@@ -79,3 +79,27 @@ def test_sparsegen_plus_processor(cuda_device):
     ref = oatt.block_sparse_attention(q, k, v, mask, 1 / 8, 64, 64)
     assert np.abs(out.double().cpu().numpy() - ref).max() <= 2e-2
     assert attn.sparsity_records[0]["records"][-1]["layer"] == 0
+
+
+def test_sparsegen_plus_warmup_pooling(cuda_device):
+    """warmup_pooling: the warm-up step returns the dense attention and keeps
+    its pooled map; the first sparse step of the layer selects its blocks by
+    the energy rule on that map (checked against the oracle's pooled map)."""
+    B, H, S, D = 1, 2, 1100, 64
+    g = torch.Generator().manual_seed(9)
+    q, k, v = (torch.randn(B, H, S, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    attn = sgp.BlockSparseAttention(layernum=1, timestep=10, warmup_epoch=1, warmup_pooling=True)
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    dense = attn(qd, kd, vd)
+    ref_o, ref_pool = oatt.attention_with_pooling(q, k, v, 1 / 8, 64)
+    assert np.abs(dense.double().cpu().numpy() - ref_o).max() <= 2e-2
+    wmap = attn.warmup_map[0].double().cpu().numpy()
+    assert np.abs(wmap - ref_pool).max() <= 2e-3
+    out = attn(qd, kd, vd)  # step 1: blocks from the warm-up map
+    assert attn.warmup_map[0] is None
+    mask = attn.mask[0].to_dense().cpu().numpy()
+    max_r, min_r, thr = attn.schedule(1)
+    ref_mask = osel.energy_select(wmap, thr, min_r, max_r, text_blocks=4)
+    assert np.array_equal(mask, ref_mask)
+    ref = oatt.block_sparse_attention(q, k, v, mask, 1 / 8, 64, 64)
+    assert np.abs(out.double().cpu().numpy() - ref).max() <= 2e-2

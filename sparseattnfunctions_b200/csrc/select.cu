@@ -52,10 +52,10 @@ struct PoolOperand {
 // block barrier, so the many small blocks cost no per-CTA synchronisation.
 // grid (ceil(B*H*max nb / 8), 1, 2): z = 0 pools q, z = 1 pools k.
 template <typename T>
-__global__ void __launch_bounds__(256) pool_mean_warp_kernel(PoolOperand q_op, PoolOperand k_op, int H,
+__global__ void __launch_bounds__(256, 3) pool_mean_warp_kernel(PoolOperand q_op, PoolOperand k_op, int H,
                                                              int D, int BH, int lpr_log2) {
   constexpr int VEC = 16 / sizeof(T);
-  constexpr int U = 8;  // row loads in flight per lane
+  constexpr int U = 6;  // row loads in flight per lane
   const PoolOperand& op = blockIdx.z == 0 ? q_op : k_op;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + warp;

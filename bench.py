@@ -390,6 +390,10 @@ def run_saf(args, world, rank, local):
                          "traffic": traffic,
                          "algorithmic_flop_per_launch": live_flops},
         }
+    if not args.no_pool:
+        pool = bench_pool(args, dev, world, q, k, v)
+        if line is not None:
+            line["pool"] = pool
     if not args.no_merge:
         merge = bench_merge(args, dev, world, rank)
         if line is not None:
@@ -403,6 +407,44 @@ def run_saf(args, world, rank, local):
         if line is not None:
             line["long"] = long_run
     return line, (q_c, k_c, v_c), csr, cfg
+
+
+def bench_pool(args, dev, world, q, k, v):
+    """Attention with the pooled attention map (attn_pooling_kernel.py, the
+    warm-up path): dense attention over the config-2 layer with and without
+    the pooled map [B, H, 139, 139]."""
+    import torch
+
+    from sparseattnfunctions_b200 import kernels
+
+    B, H, S, D = q.shape
+    nb = math.ceil(S / 128)
+    csr = kernels.mask_to_csr(torch.ones(B, H, nb, nb, dtype=torch.bool, device=dev), 128, 128)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+    n = 3
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return allreduce(e0.elapsed_time(e1) / n, "max", world)
+
+    ms_dense = timed(lambda: kernels.bsa_fwd(q, k, v, csr, 0.125, out=out))
+    ms_pool = timed(lambda: kernels.bsa_fwd_pool(q, k, v, csr, 0.125, out=out))
+    flop = 4.0 * B * H * S * S * D
+    return {"workload": "dense attention over the config-2 layer (B=2, H=30, S=17776, D=64, bf16) with the "
+                        "pooled 128-block attention map (attn_with_pooling)",
+            "ms_dense": round(ms_dense, 4), "ms_dense_with_pool": round(ms_pool, 4),
+            "pool_overhead": round(ms_pool / ms_dense - 1.0, 4),
+            "dense_tflops": round(flop / (ms_dense * 1e-3) / 1e12, 1), "steps": n}
 
 
 def bench_merge(args, dev, world, rank):
@@ -691,6 +733,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-merge", action="store_true", help="skip the config-3 ToMe sub-benchmark")
+    ap.add_argument("--no-pool", action="store_true", help="skip the attention-with-pooling sub-benchmark")
     ap.add_argument("--merge-steps", type=int, default=20)
     ap.add_argument("--no-combined", action="store_true", help="skip the config-4 combined sub-benchmark")
     ap.add_argument("--combined-steps", type=int, default=2)

@@ -33,6 +33,8 @@
 // Every mbarrier wait has a time budget; on expiry the CTA raises a shared
 // abort flag and the device status word, drains the copies and MMAs it has in
 // flight, frees TMEM and returns.
+#include <atomic>
+
 #include "saf_common.cuh"
 
 namespace saf {
@@ -44,10 +46,11 @@ constexpr int kKS = 3;         // K stages
 constexpr int kVS = 2;         // V stages
 constexpr int kThreads = 256;  // 8 warps = 2 warpgroups
 // Register split: launched at 128 per thread (2 CTAs x 256 threads per SM);
-// warpgroup 0 (producer, MMA issuer, 2 idle warps) drops to 32, the softmax
-// warpgroup (one thread per query row) rises to 224: 128*32 + 128*224 =
-// 32768 = 256*128.
-constexpr uint32_t kRegsCtl = 32, kRegsSoftmax = 224;
+// warpgroup 0 (producer and MMA issuer with the persistent tile loop, 2 idle
+// warps) drops to 56, the softmax warpgroup (one thread per query row) rises
+// to 200: 128*56 + 128*200 = 32768 = 256*128.  (32 / 224 spilled in the
+// control loop and measured 5 % slower.)
+constexpr uint32_t kRegsCtl = 56, kRegsSoftmax = 200;
 static_assert(128 * kRegsCtl + 128 * kRegsSoftmax <= kThreads * 128, "register split");
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128, kColP = 192;
@@ -78,6 +81,10 @@ struct BsaParams {
   // row's log2-sum-exp, [B*H, Sq]
   float* pool_rmax;
   float* pool_lse;
+  // persistent schedule: query tiles per head, heads, and this launch's
+  // [next tile, CTAs done] counters (zero on entry; the last CTA resets them)
+  int n_tiles, BH;
+  unsigned int* tile_ctr;
 };
 
 // Iterates the live kv tiles of one 128-row query tile.  With 64-row mask
@@ -203,8 +210,9 @@ struct Layout {
   static constexpr int kOffOnes = kOffBias + (kBias ? kVS * kBiasTile : 0);  // ones column
   static constexpr int kOffBar = kOffOnes + (kBias ? kBM * 32 : 0);
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain, b_empty[VS]
-  static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 5;
+  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain, b_empty[VS],
+  //           q_empty, tile_full[2], tile_empty[2]
+  static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 10;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
@@ -222,25 +230,24 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Launch order: the first `lead_tiles` query tiles of every head (dense
-  // text rows, the longest block lists) go first, tile-major; the rest run
-  // head-major so that CTAs resident together share a head's K/V in L2.
-  int tile, g;
-  {
-    const int n_tiles = gridDim.x, BH = gridDim.y;
-    const int lin = blockIdx.x + blockIdx.y * n_tiles;
-    const int lead = p.lead_tiles < n_tiles ? p.lead_tiles : n_tiles;
-    if (lin < lead * BH) {
-      tile = lin / BH;
-      g = lin % BH;
+  // Persistent CTAs: every CTA takes query tiles from a launch-wide counter
+  // (the producer warp fetches them and hands them to the other roles through
+  // a 2-slot ring in shared memory) until the counter passes the last tile.
+  // Tile order: the first `lead_tiles` query tiles of every head (dense text
+  // rows, the longest block lists) first, tile-major; the rest head-major so
+  // that CTAs working at the same time share a head's K/V in L2.
+  const int n_total = p.n_tiles * p.BH;
+  auto tile_of = [&](int lin, int& tile, int& g) {
+    const int lead = p.lead_tiles < p.n_tiles ? p.lead_tiles : p.n_tiles;
+    if (lin < lead * p.BH) {
+      tile = lin / p.BH;
+      g = lin % p.BH;
     } else {
-      const int rest = n_tiles - lead, l2 = lin - lead * BH;
+      const int rest = p.n_tiles - lead, l2 = lin - lead * p.BH;
       g = l2 / rest;
       tile = lead + l2 % rest;
     }
-  }
-  const int b = g / p.H, h = g % p.H;
-  const int q0 = tile * kBM;
+  };
 
   const uint32_t sQ = smem_u32(smem + L::kOffQ);
   const uint32_t sK0 = smem_u32(smem + L::kOffK);
@@ -260,8 +267,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_p_full = bar_s_full + 16;
   const uint32_t bar_pv_full = bar_s_full + 24;
   const uint32_t bar_drain = bar_s_full + 32;
+  const uint32_t bar_q_empty = bar0 + 8u * (1 + 2 * kKS + 4 * kVS + 5);
+  auto bar_tile_full = [&](int s) { return bar_q_empty + 8u * (1 + s); };
+  auto bar_tile_empty = [&](int s) { return bar_q_empty + 8u * (3 + s); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  volatile int* tile_slot = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);  // [2]
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
@@ -280,6 +291,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(bar_p_full, 128);
     mbar_init(bar_pv_full, 1);
     mbar_init(bar_drain, 1);
+    mbar_init(bar_q_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_tile_full(s), 1);
+      mbar_init(bar_tile_empty(s), 1 + 128);  // the MMA thread and the softmax threads
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -310,66 +326,90 @@ __global__ void __launch_bounds__(kThreads, 2)
     setmaxnreg_dec<kRegsCtl>();
     if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(bar_q, L::kQBytes);
-      tma_load_4d(sQ, &tm_q, bar_q, 0, q0, h, b);
-    }
-    TileIter it;
-    it.init(p, g, tile);
-    int nk = 0, nv = 0, col;  // K / V loads issued so far
+    int nk = 0, nv = 0, nq = 0, ti = 0, col;  // K / V / Q loads issued, tiles fetched
     uint32_t rm;
-    while (it.next(col, rm)) {
-      const int sk = nk % kKS, sv = nv % kVS;
-      const uint32_t pk = (nk / kKS) & 1, pv = (nv / kVS) & 1;
-      // this block's key biases (loads in flight across the K-stage wait)
-      float bvals[BN / 32];
-      if constexpr (kBias) {
-        const float* src = p.kv_bias + static_cast<int64_t>(g) * p.bias_stride;
-#pragma unroll
-        for (int i = 0; i < BN / 32; ++i) {
-          const int kv = col * BN + lane + 32 * i;
-          bvals[i] = kv < p.Sk ? src[kv] : 0.f;
-        }
-      }
-      bool ok = mbar_wait(bar_k_empty(sk), pk ^ 1, abort_flag, p.status, p.budget_ns);
+    bool ok = true;
+    while (ok) {
+      // next tile: fetched by lane 0, published in ring slot ti & 1
+      int lin = 0;
+      if (lane == 0) lin = static_cast<int>(atomicAdd(p.tile_ctr, 1u));
+      lin = __shfl_sync(0xffffffffu, lin, 0);
+      const int slot = ti & 1;
+      ok = mbar_wait(bar_tile_empty(slot), ((ti >> 1) & 1) ^ 1, abort_flag, p.status, p.budget_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(bar_k_full(sk), L::kKVBytes);
-        tma_load_4d(sK0 + sk * L::kKVBytes, &tm_k, bar_k_full(sk), 0, col * BN, h, b);
+        tile_slot[slot] = lin;
+        mbar_arrive(bar_tile_full(slot));
       }
-      if constexpr (kBias) {
-        // B rows of the bias MMA of block nk (its own 2-stage ring, freed by
-        // that MMA's commit): key row c holds bias / sm_scale in element 0
-        const int sb = nk % kVS;
-        ok = mbar_wait(bar_b_empty(sb), ((nk / kVS) & 1) ^ 1, abort_flag, p.status, p.budget_ns);
+      __syncwarp();
+      ++ti;
+      if (lin >= n_total) break;
+      int tile, g;
+      tile_of(lin, tile, g);
+      const int b = g / p.H, h = g % p.H;
+      // Q of this tile once the previous tile's QK^T products are done
+      ok = mbar_wait(bar_q_empty, (nq & 1) ^ 1, abort_flag, p.status, p.budget_ns);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_q, L::kQBytes);
+        tma_load_4d(sQ, &tm_q, bar_q, 0, tile * kBM, h, b);
+      }
+      ++nq;
+      TileIter it;
+      it.init(p, g, tile);
+      while (it.next(col, rm)) {
+        const int sk = nk % kKS, sv = nv % kVS;
+        const uint32_t pk = (nk / kKS) & 1, pv = (nv / kVS) & 1;
+        // this block's key biases (loads in flight across the K-stage wait)
+        float bvals[BN / 32];
+        if constexpr (kBias) {
+          const float* src = p.kv_bias + static_cast<int64_t>(g) * p.bias_stride;
+#pragma unroll
+          for (int i = 0; i < BN / 32; ++i) {
+            const int kv = col * BN + lane + 32 * i;
+            bvals[i] = kv < p.Sk ? src[kv] : 0.f;
+          }
+        }
+        ok = mbar_wait(bar_k_empty(sk), pk ^ 1, abort_flag, p.status, p.budget_ns);
         if (!__all_sync(0xffffffffu, ok)) break;
-        const uint32_t dst = sBias0 + sb * L::kBiasTile;
-#pragma unroll
-        for (int i = 0; i < BN / 32; ++i) {
-          const int c = lane + 32 * i;
-          const float bv = bvals[i] * p.inv_scale;
-          const uint32_t bits = kBF16 ? pack_bf16x2(bv, 0.f) : pack_f16x2(bv, 0.f);  // [bv, 0]
-          const int hv = (c >> 2) & 1;
-          st_shared_v4(dst + c * 32 + hv * 16, bits, 0u, 0u, 0u);
-          st_shared_v4(dst + c * 32 + (hv ^ 1) * 16, 0u, 0u, 0u, 0u);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar_k_full(sk), L::kKVBytes);
+          tma_load_4d(sK0 + sk * L::kKVBytes, &tm_k, bar_k_full(sk), 0, col * BN, h, b);
         }
-        fence_proxy_async_smem();
-        mbar_arrive(bar_b_full(sb));
+        if constexpr (kBias) {
+          // B rows of the bias MMA of block nk (its own 2-stage ring, freed by
+          // that MMA's commit): key row c holds bias / sm_scale in element 0
+          const int sb = nk % kVS;
+          ok = mbar_wait(bar_b_empty(sb), ((nk / kVS) & 1) ^ 1, abort_flag, p.status, p.budget_ns);
+          if (!__all_sync(0xffffffffu, ok)) break;
+          const uint32_t dst = sBias0 + sb * L::kBiasTile;
+#pragma unroll
+          for (int i = 0; i < BN / 32; ++i) {
+            const int c = lane + 32 * i;
+            const float bv = bvals[i] * p.inv_scale;
+            const uint32_t bits = kBF16 ? pack_bf16x2(bv, 0.f) : pack_f16x2(bv, 0.f);  // [bv, 0]
+            const int hv = (c >> 2) & 1;
+            st_shared_v4(dst + c * 32 + hv * 16, bits, 0u, 0u, 0u);
+            st_shared_v4(dst + c * 32 + (hv ^ 1) * 16, 0u, 0u, 0u, 0u);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(bar_b_full(sb));
+        }
+        ++nk;
+        ok = mbar_wait(bar_v_empty(sv), pv ^ 1, abort_flag, p.status, p.budget_ns);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
+          tma_load_4d(sV0 + sv * L::kKVBytes, &tm_v, bar_v_full(sv), 0, col * BN, h, b);
+        }
+        ++nv;
       }
-      ++nk;
-      ok = mbar_wait(bar_v_empty(sv), pv ^ 1, abort_flag, p.status, p.budget_ns);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
-        tma_load_4d(sV0 + sv * L::kKVBytes, &tm_v, bar_v_full(sv), 0, col * BN, h, b);
-      }
-      ++nv;
     }
     // Drain: wait for the last load issued into every stage (and so for all
     // earlier ones).  Immediate on the normal path, where the consumers have
     // already seen every load land.
     if (lane == 0) {
-      mbar_drain(bar_q, 0, p.status);
+      if (nq > 0) mbar_drain(bar_q, (nq - 1) & 1, p.status);
       for (int s = 0; s < kKS && s < nk; ++s) {
         const int last = s + ((nk - 1 - s) / kKS) * kKS;
         mbar_drain(bar_k_full(s), (last / kKS) & 1, p.status);
@@ -386,14 +426,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t kIdescQK = idesc_f16(kBM, BN, kBF16, false, false);
       constexpr uint32_t kIdescPV = idesc_f16(kBM, kD, kBF16, false, true);
       const uint32_t tS = tmem + kColS, tO = tmem + kColO, tP = tmem + kColP;
-      bool ok = mbar_wait(bar_q, 0, abort_flag, p.status, p.budget_ns);
-      tc_fence_after();
 
-      auto issue_pv = [&](int i) -> bool {
-        const int sv = i % kVS;
-        const uint32_t pv = (i / kVS) & 1;
+      // O += P V for global block jg; `first` starts the tile's accumulator.
+      auto issue_pv = [&](int jg, bool first) -> bool {
+        const int sv = jg % kVS;
+        const uint32_t pv = (jg / kVS) & 1;
         if (!mbar_wait(bar_v_full(sv), pv, abort_flag, p.status, p.budget_ns)) return false;
-        if (!mbar_wait(bar_p_full, i & 1, abort_flag, p.status, p.budget_ns)) return false;
+        if (!mbar_wait(bar_p_full, jg & 1, abort_flag, p.status, p.budget_ns)) return false;
         tc_fence_after();
         const uint32_t vbase = sV0 + sv * L::kKVBytes;
 #pragma unroll
@@ -401,48 +440,74 @@ __global__ void __launch_bounds__(kThreads, 2)
           // B = V^T: N = D (contiguous, one 128B swizzle atom), K = kv rows;
           // 16 kv rows = two 8-row atoms = 2048 bytes.
           const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, L::kKVBytes, 1024);
-          tc_mma_ts(tO, tP + kk * 8, bdesc, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_ts(tO, tP + kk * 8, bdesc, kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
         tc_commit(bar_pv_full);
         tc_commit(bar_v_empty(sv));
         return true;
       };
 
-      TileIter it;
-      it.init(p, g, tile);
-      int j = 0, col;
+      int ti = 0, nq = 0, jbase = 0, col;  // tiles taken, Q tiles used, blocks of earlier tiles
       uint32_t rm;
-      bool finished = false;
+      bool ok = true;
       while (ok) {
-        if (!it.next(col, rm)) {
-          finished = true;
+        const int slot = ti & 1;
+        if (!mbar_wait(bar_tile_full(slot), (ti >> 1) & 1, abort_flag, p.status, p.budget_ns)) break;
+        const int lin = tile_slot[slot];
+        mbar_arrive(bar_tile_empty(slot));
+        ++ti;
+        if (lin >= n_total) break;
+        int tile, g;
+        tile_of(lin, tile, g);
+        if (!mbar_wait(bar_q, nq & 1, abort_flag, p.status, p.budget_ns)) break;
+        ++nq;
+        tc_fence_after();
+        TileIter it;
+        it.init(p, g, tile);
+        int j = 0;  // blocks of this tile
+        bool finished = false;
+        while (true) {
+          if (!it.next(col, rm)) {
+            finished = true;
+            break;
+          }
+          const int jg = jbase + j;
+          const int sk = jg % kKS;
+          const uint32_t pk = (jg / kKS) & 1;
+          if (!mbar_wait(bar_k_full(sk), pk, abort_flag, p.status, p.budget_ns)) break;
+          if (!mbar_wait(bar_s_empty, (jg & 1) ^ 1, abort_flag, p.status, p.budget_ns)) break;
+          tc_fence_after();
+          const uint32_t kbase = sK0 + sk * L::kKVBytes;
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            // K-major, 128B swizzle: 16 elements of K = 32 bytes along the row.
+            const uint64_t adesc = sdesc_sw128(sQ + kk * 32, 16, 1024);
+            const uint64_t bdesc = sdesc_sw128(kbase + kk * 32, 16, 1024);
+            tc_mma_ss(tS, adesc, bdesc, kIdescQK, kk > 0 ? 1u : 0u);
+          }
+          if constexpr (kBias) {
+            const int sb = jg % kVS;
+            if (!mbar_wait(bar_b_full(sb), (jg / kVS) & 1, abort_flag, p.status, p.budget_ns)) break;
+            tc_mma_ss(tS, sdesc_sw32(sOnes, 256), sdesc_sw32(sBias0 + sb * L::kBiasTile, 256), kIdescQK, 1u);
+          }
+          tc_commit(bar_s_full);
+          tc_commit(bar_k_empty(sk));
+          if constexpr (kBias) tc_commit(bar_b_empty(jg % kVS));
+          if (j > 0 && !issue_pv(jg - 1, j == 1)) break;
+          ++j;
+        }
+        // every QK^T of the tile is issued: Q is free once they complete
+        tc_commit(bar_q_empty);
+        if (!finished) {
+          ok = false;
           break;
         }
-        const int sk = j % kKS;
-        const uint32_t pk = (j / kKS) & 1;
-        if (!mbar_wait(bar_k_full(sk), pk, abort_flag, p.status, p.budget_ns)) break;
-        if (!mbar_wait(bar_s_empty, (j & 1) ^ 1, abort_flag, p.status, p.budget_ns)) break;
-        tc_fence_after();
-        const uint32_t kbase = sK0 + sk * L::kKVBytes;
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          // K-major, 128B swizzle: 16 elements of K = 32 bytes along the row.
-          const uint64_t adesc = sdesc_sw128(sQ + kk * 32, 16, 1024);
-          const uint64_t bdesc = sdesc_sw128(kbase + kk * 32, 16, 1024);
-          tc_mma_ss(tS, adesc, bdesc, kIdescQK, kk > 0 ? 1u : 0u);
+        if (j > 0 && !issue_pv(jbase + j - 1, j == 1)) {
+          ok = false;
+          break;
         }
-        if constexpr (kBias) {
-          const int sb = j % kVS;
-          if (!mbar_wait(bar_b_full(sb), (j / kVS) & 1, abort_flag, p.status, p.budget_ns)) break;
-          tc_mma_ss(tS, sdesc_sw32(sOnes, 256), sdesc_sw32(sBias0 + sb * L::kBiasTile, 256), kIdescQK, 1u);
-        }
-        tc_commit(bar_s_full);
-        tc_commit(bar_k_empty(sk));
-        if constexpr (kBias) tc_commit(bar_b_empty(j % kVS));
-        if (j > 0 && !issue_pv(j - 1)) break;
-        ++j;
+        jbase += j;
       }
-      if (finished && j > 0) issue_pv(j - 1);
       tc_commit(bar_drain);
       mbar_drain(bar_drain, 0, p.status);
     }
@@ -471,6 +536,24 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float sl2 = p.scale_log2;
     const f2 sl2x2 = mk2(sl2, sl2);
 
+    int ti = 0, jbase = 0, col;  // tiles taken, blocks of earlier tiles
+    uint32_t rm;
+    bool ok = true;
+    while (ok) {
+    const int slot = ti & 1;
+    if (!__all_sync(0xffffffffu, mbar_wait(bar_tile_full(slot), (ti >> 1) & 1, abort_flag, p.status,
+                                            p.budget_ns))) {
+      ok = false;
+      break;
+    }
+    const int lin = tile_slot[slot];
+    mbar_arrive(bar_tile_empty(slot));
+    ++ti;
+    if (lin >= n_total) break;
+    int tile, g;
+    tile_of(lin, tile, g);
+    const int b = g / p.H, h = g % p.H;
+    const int q0 = tile * kBM;
     float m_run = -INFINITY, l_run = 0.f;
     // key intervals of this thread's query row (kRanges)
     int lo0 = 0, hi0 = 0, lo1 = 0, hi1 = 0;
@@ -482,12 +565,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     TileIter it;
     it.init(p, g, tile);
-    int j = 0, col;
-    uint32_t rm;
-    bool ok = true;
+    int j = 0;  // blocks of this tile
     while (it.next(col, rm)) {
+      const int jg = jbase + j;
       if (!__all_sync(0xffffffffu,
-                      mbar_wait(bar_s_full, j & 1, abort_flag, p.status, p.budget_ns))) {
+                      mbar_wait(bar_s_full, jg & 1, abort_flag, p.status, p.budget_ns))) {
         ok = false;
         break;
       }
@@ -537,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // before O is rescaled.
       auto wait_pv = [&]() -> bool {
         if (pv_done) return true;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status,
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_pv_full, (jg - 1) & 1, abort_flag, p.status,
                                                 p.budget_ns)))
           return false;
         tc_fence_after();
@@ -649,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool have_o =
         ok && j > 0 &&
         __all_sync(0xffffffffu,
-                   mbar_wait(bar_pv_full, (j - 1) & 1, abort_flag, p.status, p.budget_ns));
+                   mbar_wait(bar_pv_full, (jbase + j - 1) & 1, abort_flag, p.status, p.budget_ns));
     if (have_o) tc_fence_after();
     const int qrow = q0 + row;
     const float inv_l = 1.f / l_run;
@@ -684,8 +766,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
+    jbase += j;
+    }  // tile loop
     tc_fence_before();
     named_barrier_sync(1, kThreads);
+  }
+  // The last CTA to finish resets this launch's tile counters.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.tile_ctr + 1, 1u) == gridDim.x - 1) {
+      p.tile_ctr[0] = 0u;
+      p.tile_ctr[1] = 0u;
+      __threadfence();
+    }
   }
 }
 
@@ -711,13 +804,43 @@ int32_t make_qkv_map(CUtensorMap* map, const saf_tensor4* t, int rows) {
   return r == CUDA_SUCCESS ? SAF_OK : SAF_ERR_STRIDE;
 }
 
+// Tile counters of the persistent schedule: 64 launch slots of [next tile,
+// CTAs done] per device, taken round-robin by the launches (a launch leaves
+// its slot at zero when its last CTA exits, so launches 64 apart -- or
+// ordered on one stream -- never share a live slot).
+__device__ unsigned int g_tile_ctr[64 * 2];
+constexpr int kMaxDevices = 64;
+std::atomic<unsigned int> g_launch_seq{0};
+unsigned int* g_ctr_base[kMaxDevices] = {};
+
+int32_t tile_counter_slot(unsigned int** out) {
+  int dev = 0;
+  SAF_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return SAF_ERR_UNSUPPORTED;
+  if (g_ctr_base[dev] == nullptr) {
+    void* ptr = nullptr;
+    SAF_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_tile_ctr));
+    g_ctr_base[dev] = static_cast<unsigned int*>(ptr);
+  }
+  *out = g_ctr_base[dev] + 2 * (g_launch_seq.fetch_add(1u) % 64u);
+  return SAF_OK;
+}
+
 template <int BN, bool kBias, bool kBF16, bool kRanges>
 int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                       const BsaParams& p, int n_tiles, cudaStream_t stream) {
+                       BsaParams p, int n_tiles, cudaStream_t stream) {
   auto kern = bsa_fwd_sm100_kernel<BN, kBias, kBF16, kRanges>;
   const int smem = Layout<BN, kBias>::kDynSmem;
   SAF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  dim3 grid(n_tiles, p.B * p.H);
+  int dev = 0, sms = 0;
+  SAF_CUDA_TRY(cudaGetDevice(&dev));
+  SAF_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  int32_t rc = tile_counter_slot(&p.tile_ctr);
+  if (rc != SAF_OK) return rc;
+  p.n_tiles = n_tiles;
+  p.BH = p.B * p.H;
+  const int64_t total = static_cast<int64_t>(n_tiles) * p.BH;
+  const int grid = static_cast<int>(total < 2 * sms ? total : 2 * sms);  // two CTAs per SM
   kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
   SAF_CUDA_TRY(cudaGetLastError());
   return SAF_OK;

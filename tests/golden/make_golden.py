@@ -2,7 +2,7 @@
 
 Run where the reference source tree is available (it is not on the GPU box):
 
-    python tests/golden/make_golden.py [/path/to/SparseAttnFunctions]
+    python tests/golden/make_golden.py /path/to/SparseAttnFunctions
 
 It imports the reference's own Python modules from that tree -- with stub
 modules for the imports this path does not use (sageattention, torch_kmeans,
@@ -209,4 +209,6 @@ def main(root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/SparseAttnFunctions")
+    main(sys.argv[1])

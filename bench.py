@@ -439,12 +439,18 @@ def bench_pool(args, dev, world, q, k, v):
 
     ms_dense = timed(lambda: kernels.bsa_fwd(q, k, v, csr, 0.125, out=out))
     ms_pool = timed(lambda: kernels.bsa_fwd_pool(q, k, v, csr, 0.125, out=out))
+    # comparison bar only (a library kernel, not this package's path): torch's
+    # dense scaled-dot-product attention at the same shape
+    import torch.nn.functional as F
+    ms_sdpa = timed(lambda: F.scaled_dot_product_attention(q, k, v, scale=0.125))
     flop = 4.0 * B * H * S * S * D
     return {"workload": "dense attention over the config-2 layer (B=2, H=30, S=17776, D=64, bf16) with the "
                         "pooled 128-block attention map (attn_with_pooling)",
             "ms_dense": round(ms_dense, 4), "ms_dense_with_pool": round(ms_pool, 4),
             "pool_overhead": round(ms_pool / ms_dense - 1.0, 4),
-            "dense_tflops": round(flop / (ms_dense * 1e-3) / 1e12, 1), "steps": n}
+            "dense_tflops": round(flop / (ms_dense * 1e-3) / 1e12, 1),
+            "torch_sdpa_dense_ms": round(ms_sdpa, 4),
+            "torch_sdpa_dense_tflops": round(flop / (ms_sdpa * 1e-3) / 1e12, 1), "steps": n}
 
 
 def bench_merge(args, dev, world, rank):

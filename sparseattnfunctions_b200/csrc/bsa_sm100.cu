@@ -11,24 +11,32 @@
 // reference, which walks every mask bit of a row (:167-199), only the listed
 // blocks are visited.
 //
-// Design (one CTA = 128 query rows of one head, 2 CTAs per SM):
-//   warp 0      TMA producer: Q once, then K / V tiles of each live block
-//               (3-stage K ring, 2-stage V ring, 128B swizzle), plus the
-//               optional per-column bias (plain loads into shared memory).
+// Design (persistent: 2 CTAs per SM, each taking 128-row query tiles of any
+// head from a launch-wide counter until none is left):
+//   warp 0      TMA producer: fetches the next tile index and hands it to the
+//               other roles through a 2-slot ring in shared memory, loads Q
+//               once the previous tile's QK^T products are done, then K / V
+//               tiles of each live block (3-stage K ring, 2-stage V ring,
+//               128B swizzle) and, with a key bias, the block's 16-bit
+//               bias / sm_scale column tile (2-stage ring, 32B swizzle).
 //   warp 1      TMEM allocator and single-thread tcgen05.mma issuer:
-//               S = Q K^T (SS form) into TMEM, then O += P V (TS form, P read
-//               from TMEM) for the previous block.
+//               S = Q K^T (SS form) into TMEM (+ ones x bias^T: one more
+//               K = 16 MMA that adds the key bias), then O += P V (TS form, P
+//               read from TMEM) for the previous block.
 //   warps 2,3   idle (they complete warpgroup 0 for the register split).
-//   warps 4..11 softmax: two threads per query row (TMEM lane); warps 4-7
-//               take key columns [0, BN/2), warps 8-11 [BN/2, BN).  Each
-//               thread reads its half-row of S once into registers (so the
-//               next QK^T may start at once), the pair exchanges its row max
-//               through shared memory (an mbarrier, not a named barrier, so
-//               the wait keeps its time budget), and each writes its half of
-//               P (bf16/f16 pairs) into TMEM.  The running max only moves when
-//               it grows by more than 2^8 (lazy rescale: P <= 256, exact
-//               after the final 1/l); O in TMEM is rescaled only then.
-// TMEM columns: S [0,128) | O [128,192) | P [192,256).
+//   warps 4..7  softmax: one thread per query row (TMEM lane) holds the
+//               row's BN scores of a block, so the block maximum needs no
+//               exchange; the scores are read once into registers (so the
+//               next QK^T may start at once) and P (bf16/f16 pairs) is
+//               written into TMEM.  P is computed speculatively with the
+//               running max; the max only moves when it grows by more than
+//               2^8 (lazy rescale: P <= 256, exact after the final 1/l), and
+//               then P is recomputed and O rescaled in TMEM.  Each tile ends
+//               with O read back, normalised and stored by these warps.
+//               Optionally (attention with a pooled map) they also store each
+//               row's block maxima and log2-sum-exp.
+// TMEM columns: S [0,128) | O [128,192) | P [192,256).  Block phases of all
+// rings run on a block counter that continues across a CTA's tiles.
 //
 // Every mbarrier wait has a time budget; on expiry the CTA raises a shared
 // abort flag and the device status word, drains the copies and MMAs it has in

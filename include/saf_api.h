@@ -5,6 +5,8 @@
  * (passed as `void*`, a cudaStream_t), returns a saf_status, allocates no
  * device memory and never synchronises the device (except the functions
  * documented as synchronising).  All work is enqueued on the given stream.
+ * An entry point runs on the device that owns its tensors and leaves the
+ * calling thread's current CUDA device as it found it.
  *
  * The reference (xiaolong-li1/SparseAttnFunctions, Python + Triton) has no
  * FFI; the Python host package `sparseattnfunctions_b200.special_attentions`
@@ -164,6 +166,12 @@ int32_t saf_energy_select(const double* in, int32_t is_mass, int64_t BH, int32_t
  * all others -- pass the number of dense (text) rows, whose block lists are
  * the longest, so they do not start last and stretch the tail; 0 keeps
  * head-major order.  Results do not depend on it.
+ * Each launch takes one of 64 per-device tile-counter slots, round-robin
+ * at launch time, and leaves it at zero when it ends: launches ordered on
+ * one stream, or fewer than 64 in flight at once, never share a live slot.
+ * A launch captured in a CUDA graph keeps its slot for every replay, so a
+ * replay must not overlap other attention launches of this library on the
+ * same device.
  * Replaces: _forward / _fwd_kernel / _fwd_kernel_inner /
  * block_sparse_triton_fn (utils/block_sparse_attn_kernel.py:52-293) and the
  * bias path of MergeAttention.forward (MergeAttention.py:33-49). */

@@ -63,6 +63,38 @@ def block_sparse_attention(q, k, v, block_mask, sm_scale: float, block_m: int, b
     return out
 
 
+def block_sparse_attention_rows(q, k, v, block_mask, sm_scale: float, block_m: int, block_n: int,
+                                heads: Iterable[int], rows: Iterable[int]) -> np.ndarray:
+    """The same fp64 definition as ``block_sparse_attention`` evaluated only
+    for the query ``rows`` of the flat heads ``heads`` (b*H + h), for
+    sampled parity checks at full sequence lengths.  Returns float64
+    ``[len(heads), len(rows), D]`` (NaN for a row with no live block)."""
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    rows = np.asarray(list(rows), dtype=np.int64)
+    heads = list(heads)
+    mask = block_mask
+    out = np.full((len(heads), rows.size, D), np.nan, dtype=np.float64)
+    for hi, g in enumerate(heads):
+        b, h = divmod(int(g), H)
+        qh = to_f64(q[b, h])
+        kh = to_f64(k[b, h])
+        vh = to_f64(v[b, h])
+        mh = np.asarray(to_f64(mask[b, h]) != 0)
+        for i in np.unique(rows // block_m):
+            sel = np.nonzero(rows // block_m == i)[0]
+            cols = np.nonzero(mh[i])[0]
+            if cols.size == 0:
+                continue
+            kv_idx = np.concatenate([np.arange(c * block_n, min(Sk, (c + 1) * block_n)) for c in cols])
+            logits = (qh[rows[sel]] @ kh[kv_idx].T) * sm_scale
+            logits -= logits.max(axis=1, keepdims=True)
+            p = np.exp(logits)
+            p /= p.sum(axis=1, keepdims=True)
+            out[hi, sel] = p @ vh[kv_idx]
+    return out
+
+
 def attention_with_pooling(q, k, v, sm_scale: float, block_size: int, block_mask=None):
     """fp64 attention with the pooled attention map of
     special_attentions/utils/attn_pooling_kernel.py (non-causal path).

@@ -187,3 +187,14 @@ def read_device_status(device: int, clear: bool = True) -> int:
     flags = ctypes.c_uint32(0)
     check("saf_read_device_status", load().saf_read_device_status(device, ctypes.byref(flags), int(clear)))
     return int(flags.value)
+
+
+def raise_on_device_status(device: int) -> None:
+    """Reads and clears ``device``'s status flags; raises ``SafTimeoutError``
+    when a device-side wait ran out and ``SafError`` when a kernel skipped an
+    out-of-range index."""
+    flags = read_device_status(device, clear=True)
+    if flags & SAF_DEV_TIMEOUT:
+        raise SafTimeoutError("device status", SAF_ERR_TIMEOUT, f"a device wait ran out (flags {flags:#x})")
+    if flags:
+        raise SafError("device status", SAF_ERR_ARG, f"a kernel skipped an out-of-range index (flags {flags:#x})")

@@ -282,7 +282,8 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (q->dtype == SAF_F32) {
     if (pool_rmax != nullptr || pool_lse != nullptr) return SAF_ERR_UNSUPPORTED;
-    if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
+    DeviceScope dev_scope;
+    if ((rc = dev_scope.bind(q->data)) != SAF_OK) return rc;
     return bsa_fwd_simt(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                         kv_bias_stride_bh, sm_scale, row_ranges, st);
   }
@@ -296,7 +297,8 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
         (t->stride_b * 2) % 16 != 0)
       return SAF_ERR_STRIDE;
   }
-  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(q->data)) != SAF_OK) return rc;
   // Leading mask rows -> leading 128-row query tiles scheduled first.
   const int64_t lead_tiles = (static_cast<int64_t>(lead_rows) * block_m + 127) / 128;
   return bsa_fwd_sm100(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,

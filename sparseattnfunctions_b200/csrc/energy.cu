@@ -128,7 +128,8 @@ extern "C" int32_t saf_energy_select(const double* in, int32_t is_mass, int64_t 
     return SAF_ERR_SHAPE;
   if (min_retain < 0 || max_retain < 0 || text_blocks < 0) return SAF_ERR_ARG;
   int32_t rc;
-  if ((rc = bind_device_of(in)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(in)) != SAF_OK) return rc;
   EnergyParams p{in, is_mass != 0, BH * nbq, nbq, nbk, block_n, static_cast<int>(Sk), scale, threshold,
                  min_retain, max_retain, text_blocks, mass_out, mask};
   const int64_t rows = BH * nbq;

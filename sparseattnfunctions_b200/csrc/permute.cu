@@ -76,7 +76,8 @@ extern "C" int32_t saf_permute_tokens(const void* x, void* out, int32_t dtype, i
                    (reinterpret_cast<uintptr_t>(out) & 15) == 0 && x_sb % v == 0 && x_sh % v == 0 &&
                    x_ss % v == 0 && o_sb % v == 0 && o_sh % v == 0 && o_ss % v == 0;
   int32_t rc;
-  if ((rc = bind_device_of(x)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(x)) != SAF_OK) return rc;
   const int64_t div = vec ? v : 1;
   PermuteParams p{x, out, x_sb / div, x_sh / div, x_ss / div, o_sb / div, o_sh / div, o_ss / div,
                   perm, heads, static_cast<int>(H), static_cast<int>(S), static_cast<int>(S_out),

@@ -98,7 +98,8 @@ extern "C" int32_t saf_bsa_fwd_pool(const saf_tensor4* q, const saf_tensor4* k, 
   float* rmax = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   float* lse = rmax + BH * nbk * Sq;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(q->data)) != SAF_OK) return rc;
   const int64_t n_r = BH * nbk * Sq;
   fill_kernel<<<static_cast<unsigned>(std::min<int64_t>((n_r + 255) / 256, 148 * 32)), 256, 0, st>>>(
       rmax, n_r, -INFINITY);

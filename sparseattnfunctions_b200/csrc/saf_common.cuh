@@ -34,9 +34,20 @@ CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32
                            const cuuint32_t* box, CUtensorMapSwizzle swizzle);
 // Current device is sm_100 (B200 family).
 bool current_device_is_sm100();
-// Makes the device that owns `ptr` current for this library's runtime (the
-// caller's runtime -- e.g. PyTorch's -- keeps its own current device).
-int32_t bind_device_of(const void* ptr);
+// Makes the device that owns a pointer current for one entry point and puts
+// the calling thread's previous current device back when the scope ends, so
+// a C caller's later runtime calls land on the device it had selected.
+class DeviceScope {
+ public:
+  DeviceScope() = default;
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+  ~DeviceScope();
+  int32_t bind(const void* ptr);
+
+ private:
+  int prev_ = -1;  // device to restore, or -1 when nothing was changed
+};
 
 inline int elem_bytes(int32_t dtype) { return dtype == SAF_F32 ? 4 : 2; }
 

@@ -73,7 +73,7 @@ bool current_device_is_sm100() {
   return major == 10 && minor == 0;
 }
 
-int32_t bind_device_of(const void* ptr) {
+int32_t DeviceScope::bind(const void* ptr) {
   cudaPointerAttributes attr;
   if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
     cudaGetLastError();
@@ -82,8 +82,15 @@ int32_t bind_device_of(const void* ptr) {
   if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) return SAF_ERR_ARG;
   int cur = -1;
   if (cudaGetDevice(&cur) != cudaSuccess) return SAF_ERR_CUDA;
-  if (cur != attr.device && cudaSetDevice(attr.device) != cudaSuccess) return SAF_ERR_CUDA;
+  if (cur != attr.device) {
+    if (cudaSetDevice(attr.device) != cudaSuccess) return SAF_ERR_CUDA;
+    if (prev_ < 0) prev_ = cur;
+  }
   return SAF_OK;
+}
+
+DeviceScope::~DeviceScope() {
+  if (prev_ >= 0) cudaSetDevice(prev_);
 }
 
 namespace {

@@ -523,7 +523,8 @@ extern "C" int32_t saf_pool_topk(const saf_tensor4* q, const saf_tensor4* k,
   const SelectLayout lay = select_layout(BH, nbq, nbk, D);
   if (workspace == nullptr || workspace_bytes < lay.total) return SAF_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return SAF_ERR_WORKSPACE;
-  if ((rc = bind_device_of(q->data)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(q->data)) != SAF_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   double* qbar = reinterpret_cast<double*>(ws + lay.off_qbar);
@@ -566,7 +567,8 @@ extern "C" int32_t saf_mask_to_csr(const uint8_t* mask, int64_t BH, int32_t nbq,
   if (BH * static_cast<int64_t>(nbq) * nbk >= (int64_t(1) << 31)) return SAF_ERR_SHAPE;
   if (stride_row < nbk || stride_bh < 0) return SAF_ERR_STRIDE;
   if (BH > 2147483647) return SAF_ERR_SHAPE;
-  int32_t rc = bind_device_of(mask);
+  DeviceScope dev_scope;
+  int32_t rc = dev_scope.bind(mask);
   if (rc != SAF_OK) return rc;
   const size_t smem = (static_cast<size_t>(nbq) + 1) * sizeof(int32_t);
   mask_to_csr_kernel<<<static_cast<unsigned>(BH), 512, smem, static_cast<cudaStream_t>(stream)>>>(
@@ -625,7 +627,8 @@ extern "C" int32_t saf_pool_topk_noalloc(const saf_tensor4* q, const saf_tensor4
   const size_t need = saf_pool_topk_workspace_bytes(q, k, cfg);
   if (need == 0) return SAF_ERR_ARG;
   if (need > SAF_STATIC_SCRATCH_BYTES) return SAF_ERR_WORKSPACE;  // problem too large for it
-  int32_t rc = bind_device_of(q->data);
+  DeviceScope dev_scope;
+  int32_t rc = dev_scope.bind(q->data);
   if (rc != SAF_OK) return rc;
   void* scratch = nullptr;
   if ((rc = static_scratch_address(&scratch)) != SAF_OK) return rc;

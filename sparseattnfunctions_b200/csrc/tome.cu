@@ -940,7 +940,8 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   if (workspace == nullptr || workspace_bytes < lay.total ||
       (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return SAF_ERR_WORKSPACE;
-  int32_t rc = bind_device_of(metric);
+  DeviceScope dev_scope;
+  int32_t rc = dev_scope.bind(metric);
   if (rc != SAF_OK) return rc;
   if (!current_device_is_sm100()) return SAF_ERR_UNSUPPORTED;
   unsigned int* status = device_status_ptr();
@@ -1157,7 +1158,8 @@ extern "C" int32_t saf_tome_kv_metric(const saf_tensor4* k, const saf_tensor4* v
         x->stride_b % 2)
       return SAF_ERR_STRIDE;
   if ((reinterpret_cast<uintptr_t>(out) & 3) != 0) return SAF_ERR_STRIDE;
-  if ((rc = bind_device_of(k->data)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(k->data)) != SAF_OK) return rc;
   KvMetricParams p{k->data, v->data, out, k->stride_b, k->stride_h, k->stride_s, v->stride_b,
                    v->stride_h, v->stride_s, static_cast<int>(k->H), static_cast<int>(k->S),
                    static_cast<int>(k->D), text_len};
@@ -1185,7 +1187,8 @@ extern "C" int32_t saf_tome_merge(const void* x, void* out, int32_t dtype, int64
     return SAF_ERR_SHAPE;
   if (r < Ns && plan->unm_idx == nullptr) return SAF_ERR_ARG;
   if (x_stride_n < C || o_stride_n < C) return SAF_ERR_STRIDE;
-  if ((rc = bind_device_of(x)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(x)) != SAF_OK) return rc;
   RowCopyParams q{x, out, x_stride_b, x_stride_n, o_stride_b, o_stride_n, static_cast<int>(B),
                   static_cast<int>(C), text_len, static_cast<int>(Ns), static_cast<int>(Nd), r, 0,
                   a_idx, b_idx, plan->unm_idx, plan->counter, plan->dst_ptr, plan->dst_src, nullptr};
@@ -1223,7 +1226,8 @@ extern "C" int32_t saf_tome_unmerge(const void* y, void* out, int32_t dtype, int
   if (token_map == nullptr) return SAF_ERR_ARG;
   if (B <= 0 || C <= 0 || N <= 0 || text_len < 0 || B > 65535) return SAF_ERR_SHAPE;
   if (y_stride_n < C || o_stride_n < C) return SAF_ERR_STRIDE;
-  if ((rc = bind_device_of(y)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(y)) != SAF_OK) return rc;
   RowCopyParams q{y, out, y_stride_b, y_stride_n, o_stride_b, o_stride_n, static_cast<int>(B),
                   static_cast<int>(C), text_len, 0, 0, 0, static_cast<int>(N), nullptr, nullptr,
                   nullptr, nullptr, nullptr, nullptr, token_map};

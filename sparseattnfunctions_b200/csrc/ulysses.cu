@@ -111,7 +111,8 @@ int32_t ulysses_launch(bool pack, void* const* seq, int32_t T, int32_t dtype, in
   p.vec = static_cast<int32_t>(D * elem / 16);
   if (s == 0) return SAF_OK;
   int32_t rc;
-  if ((rc = bind_device_of(buf)) != SAF_OK) return rc;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(buf)) != SAF_OK) return rc;
   const int64_t most = s * B * T * static_cast<int64_t>(hmax) * p.vec;  // vectors of the largest chunk
   if (most == 0) return SAF_OK;
   if (most >= (int64_t(1) << 31)) return SAF_ERR_SHAPE;

@@ -109,12 +109,22 @@ class BlockSparseAttention:
         csr = self.select(q, k, step, layer)
         self.mask[layer] = csr
         out = kernels.bsa_fwd(q, k, v, csr, self.sm_scale)
-        sparsity = 1.0 - float(csr.nnz_per_head().sum()) / (csr.B * csr.H * csr.nbq * csr.nbk)
+        sparsity = self._calculate_sparsity(csr)
         sample = self.counter // (self.layernum * self.timestep)
         if sample < len(self.sparsity_records):
             self.sparsity_records[sample]["records"].append(
                 {"timestep": step, "layer": layer, "sparsity": sparsity})
         return out
+
+    @staticmethod
+    def _calculate_sparsity(csr: kernels.BlockCSR) -> float:
+        """The reference's record (SparseGen_Plus.py:136-141): the fraction of
+        dead blocks; with a batch of one it is blended as if the heads were
+        H of 96 with the remaining 96 - H at 0.9."""
+        dead = 1.0 - float(csr.nnz_per_head().sum()) / (csr.B * csr.H * csr.nbq * csr.nbk)
+        if csr.B == 1:
+            return (dead * csr.H + 0.9 * (96 - csr.H)) / 96
+        return dead
 
     def dense(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer: int = 0) -> torch.Tensor:
         bs = self.block_size

@@ -19,15 +19,20 @@ import math
 
 import torch
 
-from .. import kernels
+from .. import _lib, kernels
 from ..geometry import COGVIDEOX_2B, VideoGeometry
 
 
 class BlockSparseAttention:
     def __init__(self, block_size: int = 128, density: float = 0.10,
                  geometry: VideoGeometry = COGVIDEOX_2B, text_dense: bool = True,
-                 sm_scale: float | None = None):
+                 sm_scale: float | None = None, check_status: bool = False):
+        """``check_status``: after every call, synchronise the device and
+        raise ``SafTimeoutError`` (a kernel wait ran out) or ``SafError`` (an
+        index was out of range and skipped) if the device status word is
+        set.  Off by default: it costs a host synchronisation per call."""
         super().__init__()
+        self.check_status = check_status
         self.block_size = block_size
         self.density = density
         self.geometry = geometry
@@ -49,7 +54,10 @@ class BlockSparseAttention:
         scale = self.sm_scale if self.sm_scale is not None else 1.0 / math.sqrt(q.shape[-1])
         csr = self.select(q, k)
         self.last_csr = csr
-        return kernels.bsa_fwd(q, k, v, csr, scale, out=out)
+        out = kernels.bsa_fwd(q, k, v, csr, scale, out=out)
+        if self.check_status:
+            _lib.raise_on_device_status(q.device.index)
+        return out
 
     def __call__(self, q, k, v, out=None):
         return self.forward(q, k, v, out=out)

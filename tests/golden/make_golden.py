@@ -24,6 +24,14 @@ Fixtures
                     its per-frame key sets at CogVideoX-2B size, and the
                     process / process_back token orders (SmartAttention.py:
                     9-43, 90-95)
+  attention_kat.npz block-sparse attention as the reference's own test oracle
+                    defines it (the kron-mask statements of
+                    test_topk_sparse_attention and
+                    test_topk_sparse_attention_qlt_kl,
+                    block_sparse_attn_kernel.py:326-334 and 366-384), run in
+                    fp64 on the KAT shapes, a ragged case with an empty row
+                    and the config-1 shape; stored as per-row sums and a
+                    fixed random projection of each output row
 """
 from __future__ import annotations
 
@@ -116,6 +124,121 @@ def smart_layout(root: str):
     return out
 
 
+class _CpuTorch:
+    """The torch namespace for the reference's test-oracle statements: every
+    attribute is torch's own, except that tensor factories given
+    ``device='cuda'`` (the reference's tests run on a GPU) build CPU
+    tensors."""
+
+    def __init__(self):
+        import torch
+
+        self._torch = torch
+
+    def __getattr__(self, name):
+        attr = getattr(self._torch, name)
+        if name in ("ones", "zeros", "arange", "full", "randn", "rand"):
+            def factory(*args, **kwargs):
+                if str(kwargs.get("device", "cpu")).startswith("cuda"):
+                    kwargs["device"] = "cpu"
+                return attr(*args, **kwargs)
+            return factory
+        return attr
+
+
+def reference_kat_oracles(root: str):
+    """The reference's own test-oracle statements as callables: the slice of
+    ``test_topk_sparse_attention`` from ``full_mask = ...`` to ``ref_output
+    = ...`` (block_sparse_attn_kernel.py:326-334) and of
+    ``test_topk_sparse_attention_qlt_kl`` from ``past_len = ...`` to
+    ``ref_output = ...`` (:366-384), taken from the source text and run with
+    the inputs as arguments."""
+    import ast
+    import torch
+
+    src = Path(root, "special_attentions", "utils", "block_sparse_attn_kernel.py").read_text()
+    fns = {n.name: n for n in ast.parse(src).body if isinstance(n, ast.FunctionDef)}
+
+    def assigned(st):
+        return [t.id for t in getattr(st, "targets", []) if isinstance(t, ast.Name)]
+
+    def make(fname, first, args):
+        body = fns[fname].body
+        i0 = next(i for i, st in enumerate(body) if first in assigned(st))
+        i1 = next(i for i, st in enumerate(body) if i >= i0 and "ref_output" in assigned(st))
+        stmts = body[i0:i1 + 1] + [ast.Return(value=ast.Name("ref_output", ast.Load()))]
+        fn = ast.FunctionDef(name="kat_oracle", args=ast.arguments(
+            posonlyargs=[], args=[ast.arg(a) for a in args], kwonlyargs=[], kw_defaults=[], defaults=[]),
+            body=stmts, decorator_list=[], returns=None, type_params=[])
+        mod = ast.fix_missing_locations(ast.Module(body=[fn], type_ignores=[]))
+        ns = {"torch": _CpuTorch(), "F": torch.nn.functional}
+        exec(compile(mod, f"{fname}-oracle", "exec"), ns)
+        return ns["kat_oracle"]
+
+    square = make("test_topk_sparse_attention", "full_mask", ["q", "k", "v", "block_mask", "sm_scale", "BLOCK",
+                                                              "SEQ_LEN"])
+    rect = make("test_topk_sparse_attention_qlt_kl", "past_len", ["q", "k", "v", "block_mask", "sm_scale",
+                                                                  "BLOCK", "Q_LEN", "K_LEN"])
+    return square, rect
+
+
+# (name, seed, B, H, Sq, Sk, block, topk or None for all-ones, force first column, empty row)
+ATTN_CASES = [("kat_ragged_ones", 301, 1, 3, 257, 257, 64, None, True, -1),
+              ("kat_ragged_top2", 302, 1, 3, 257, 257, 64, 2, True, -1),
+              ("kat_qlen_lt_klen", 303, 2, 4, 128, 256, 64, 1, True, -1),
+              ("ragged_empty_row", 304, 2, 2, 300, 300, 64, 2, False, 3),
+              ("config1_shape", 305, 1, 2, 2048, 2048, 64, 8, True, -1)]
+
+
+def attn_inputs(seed, B, H, Sq, Sk, block, topk, force_first, empty_row, bsk=None):
+    """Seeded fp64 q, k, v (N(0,1) / 8 for q and k) and the block mask.  The
+    mask is the reference's get_sparse_attn_mask_from_topk of seeded scores
+    (first column forced high like the reference's KAT); it is computed by
+    the reference when ``bsk`` is given, else read back from the fixture."""
+    import torch
+
+    rs = np.random.RandomState(seed)
+    q = rs.randn(B, H, Sq, 64) / 8.0
+    k = rs.randn(B, H, Sk, 64) / 8.0
+    v = rs.randn(B, H, Sk, 64)
+    nbq, nbk = -(-Sq // block), -(-Sk // block)
+    n = max(nbq, nbk)
+    x = rs.randn(B, H, n, n)
+    if force_first:
+        x[..., 0] = 100.0
+    if bsk is None:
+        return q, k, v, None
+    if topk is None:
+        mask = torch.ones(B, H, n, n, dtype=torch.bool)
+    else:
+        mask = bsk.get_sparse_attn_mask_from_topk(torch.from_numpy(x), topk)
+    if empty_row >= 0:
+        mask[0, 0, empty_row, :] = False
+    return q, k, v, mask
+
+
+def attention_kat(root: str, bsk):
+    import torch
+
+    square, rect = reference_kat_oracles(root)
+    out = {"cases": np.array([[-1 if x is None else int(x) for x in c[1:]] for c in ATTN_CASES],
+                             dtype=np.int64)}
+    for name, seed, B, H, Sq, Sk, block, topk, ff, er in ATTN_CASES:
+        q, k, v, mask = attn_inputs(seed, B, H, Sq, Sk, block, topk, ff, er, bsk)
+        tq, tk, tv = (torch.from_numpy(t) for t in (q, k, v))
+        if Sq == Sk:
+            ref = square(tq, tk, tv, mask, 0.125, block, Sq)
+        else:
+            ref = rect(tq, tk, tv, mask, 0.125, block, Sq, Sk)
+        ref = ref.numpy()
+        proj = np.random.RandomState(seed + 3000).randn(64)
+        out[f"{name}_mask"] = np.packbits(mask.numpy())
+        out[f"{name}_mask_shape"] = np.array(mask.shape)
+        out[f"{name}_rowsum"] = ref.sum(-1)
+        out[f"{name}_proj"] = ref @ proj
+    return out
+
+
 def closure_vars(fn):
     return {name: cell.cell_contents for name, cell in zip(fn.__code__.co_freevars, fn.__closure__)}
 
@@ -203,6 +326,7 @@ def main(root: str):
         out["unmerge_rowsum"] = un.sum(-1).reshape(-1).numpy()
         out["unmerge_proj"] = (un @ proj).reshape(-1).numpy()
         np.savez_compressed(HERE / f"{name}.npz", **out)
+    np.savez_compressed(HERE / "attention_kat.npz", **attention_kat(root, bsk))
     np.savez_compressed(HERE / "smart_layout.npz", **smart_layout(root))
     np.savez_compressed(HERE / "sta_layout.npz", **sta_layout(root))
     print("fixtures written to", HERE)

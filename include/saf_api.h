@@ -152,6 +152,18 @@ int32_t saf_energy_select(const double* in, int32_t is_mass, int64_t BH, int32_t
                           int32_t min_retain, int32_t max_retain, int32_t text_blocks,
                           double* mass_out, uint8_t* mask, void* stream);
 
+/* Adaptive top-k block selection on the same input: per row, with the mass
+ * sorted descending (ties to the lower column) and E = the fp64 running sum
+ * of the first init_k blocks, k = init_k; if E < 0.6 x total, k = min(3k,
+ * nbk); then if E < 0.9 x total, k = min(k / 3 * 2, nbk) (integer division,
+ * on the updated k); the first k sorted blocks are kept and rows / columns
+ * < text_blocks forced.  1 <= init_k <= nbk (the caller turns a fraction
+ * into a count as the reference does: int(nbk * init_k)).
+ * Replaces: transfer_attn_to_mask(mode="topk") (SparseGen_Plus.py:28-50). */
+int32_t saf_topk_adaptive_select(const double* in, int32_t is_mass, int64_t BH, int32_t nbq,
+                                 int32_t nbk, int32_t block_n, int64_t Sk, double scale, int32_t init_k,
+                                 int32_t text_blocks, double* mass_out, uint8_t* mask, void* stream);
+
 /* ---- (2) block-sparse attention -------------------------------------
  * o[b,h,i,:] = sum_{j live} softmax_j(sm_scale * q_i . k_j + bias_j) v_j
  * over the key blocks listed in the CSR row of query block i / block_m.
@@ -193,6 +205,56 @@ int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k, const saf
                            int64_t col_capacity, int32_t block_m, int32_t block_n,
                            const float* kv_bias, int64_t kv_bias_stride_bh, float sm_scale,
                            int32_t lead_rows, const int32_t* row_ranges, void* stream);
+
+/* ---- frame-scope masks (frame x frame sparsity on the unpadded sequence)
+ * The sequence is [text_len text tokens | frames x frame_len video tokens].
+ *
+ * saf_frame_mask: the frame x frame attention map of a sampled subset --
+ * every text token and, in every frame, the same n spatial positions
+ * spatial[0..n) (int32 in [0, frame_len)) -- and its per-head 90 %-style
+ * energy mask.  logits = sm_scale * q_s . k_s (+ log(n / frame_len), as a
+ * float32, on the text keys), softmax over the sampled keys, map[f1, f2] =
+ * the video-video probability of frame pair (f1, f2) summed over the frame's
+ * sampled queries / n; per head the flattened map sorted in descending
+ * order keeps every entry ranked at or before the first position whose
+ * cumulative sum reaches threshold x the total.  Outputs: bits_out [B*H,
+ * frames] uint32 (bit f2 of word f1 = frame f2 visible to frame f1),
+ * optional mask_out [B*H, frames, frames] uint8 and map_out fp64.
+ * frames <= 32, n <= frame_len, D = 64 or 128; workspace of
+ * saf_frame_mask_workspace_bytes.  An out-of-range spatial entry sets
+ * SAF_DEV_BADINDEX and reads position 0.
+ * Replaces: generate_attention_mask_frame_scope
+ * (utils/mask_related.py:194-245), which draws the spatial sample itself. */
+size_t saf_frame_mask_workspace_bytes(int64_t BH, int32_t frames, int32_t n, int32_t text_len,
+                                      int32_t D);
+int32_t saf_frame_mask(const saf_tensor4* q, const saf_tensor4* k, const int32_t* spatial, int32_t n,
+                       int32_t text_len, int32_t frames, int32_t frame_len, float sm_scale,
+                       double threshold, void* workspace, size_t workspace_bytes, double* map_out,
+                       uint8_t* mask_out, uint32_t* bits_out, void* stream);
+
+/* Frame masks -> segmented CSR over block_m x block_n blocks of the
+ * unpadded sequence (S = text_len + frames x frame_len, frames < 32,
+ * frame_len >= block_n): a query block holding a text row lists every key
+ * block; any other lists the key blocks holding a text key or a key of a
+ * frame that one of its frames sees.
+ * Replaces: get_block_mask (utils/mask_related.py:397-404), whose kron of
+ * the frame mask with a per-frame block mask needs frame-aligned padding. */
+int32_t saf_frame_csr(const uint32_t* bits, int64_t BH, int32_t text_len, int32_t frames,
+                      int32_t frame_len, int64_t S, int32_t block_m, int32_t block_n, int32_t* row_ptr,
+                      int32_t* col_idx, void* stream);
+
+/* saf_bsa_fwd under frame masks: inside every visited block, a video query
+ * of frame f1 of head g sees only the text keys and the keys of the frames
+ * set in frame_bits[g * frames + f1]; text queries see every key.  16-bit
+ * inputs, Sq = Sk = text_len + frames x frame_len, frame_len >= block_n.
+ * Replaces: block_sparse_triton_fn on the padded and randomly truncated
+ * layout of BlockSparseAttention.forward_backup (block_mask_attn.py:11-20,
+ * utils/mask_related.py:87-187). */
+int32_t saf_bsa_fwd_frames(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                           const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
+                           int64_t col_capacity, int32_t block_m, int32_t block_n,
+                           const uint32_t* frame_bits, int32_t text_len, int32_t frames,
+                           int32_t frame_len, float sm_scale, int32_t lead_rows, void* stream);
 
 /* Attention with a pooled attention map.  Runs the block-sparse attention
  * (16-bit inputs, no key bias) and writes pool_out [B*H, nbp, nbk] fp32,

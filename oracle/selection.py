@@ -141,6 +141,33 @@ def energy_select(attn: np.ndarray, energy_threshold: float, min_retain_ratio: f
     return mask
 
 
+def topk_adaptive_select(attn: np.ndarray, init_k, text_blocks: int = 4) -> np.ndarray:
+    """Restatement of transfer_attn_to_mask(mode="topk")
+    (special_attentions/SparseGen_Plus.py:28-50) on a square map: k0 =
+    int(n * init_k) for a fraction, else int(init_k); E = cumulative sum of
+    the first k0 sorted values; rows with E < 0.6 total go to min(3 k0, n),
+    then rows with E < 0.9 total to min(k // 3 * 2, n); the first k sorted
+    blocks are kept; text rows / columns forced."""
+    B, H, n, _ = attn.shape
+    k0 = int(n * init_k) if init_k < 1 else int(init_k)
+    order = np.argsort(-attn, axis=-1, kind="stable")
+    srt = np.take_along_axis(attn, order, axis=-1)
+    cum = np.cumsum(srt, axis=-1)
+    total = cum[..., -1]
+    e = cum[..., k0 - 1]
+    k = np.full(attn.shape[:-1], k0, dtype=np.int64)
+    grow = ~(e >= 0.6 * total) & (k < n)
+    cut = ~(e >= 0.9 * total) & (k < n)
+    k = np.where(grow, np.minimum(3 * k, n), k)
+    k = np.where(cut, np.minimum(k // 3 * 2, n), k)
+    keep_sorted = np.arange(n)[None, None, None, :] < k[..., None]
+    mask = np.zeros(attn.shape, dtype=bool)
+    np.put_along_axis(mask, order, keep_sorted, axis=-1)
+    mask[:, :, :text_blocks, :] = True
+    mask[:, :, :, :text_blocks] = True
+    return mask
+
+
 def dense_to_csr(mask: np.ndarray):
     """Dense bool [B,H,nbq,nbk] -> (row_ptr [B*H, nbq+1], col_idx) in the
     library's segmented layout (head g's entries start at g*nbq*nbk)."""

@@ -112,11 +112,19 @@ SIGNATURES = {
     "saf_pool_topk_noalloc": (_I32, [_PT4, _PT4, _PCFG, _P, _P, _P, _P, _P]),
     "saf_energy_select": (_I32, [_P, _I32, _I64, _I32, _I32, _I32, _I64, ctypes.c_double, ctypes.c_double,
                                  _I32, _I32, _I32, _P, _P, _P]),
+    "saf_topk_adaptive_select": (_I32, [_P, _I32, _I64, _I32, _I32, _I32, _I64, ctypes.c_double, _I32, _I32,
+                                        _P, _P, _P]),
     "saf_mask_to_csr": (_I32, [_P, _I64, _I32, _I32, _I64, _I64, _P, _P, _P]),
     "saf_bsa_fwd": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I64, _F32, _I32,
                            _P]),
     "saf_bsa_fwd_ranges": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I64, _F32,
                                   _I32, _P, _P]),
+    "saf_frame_mask_workspace_bytes": (_SZ, [_I64, _I32, _I32, _I32, _I32]),
+    "saf_frame_mask": (_I32, [_PT4, _PT4, _P, _I32, _I32, _I32, _I32, _F32, ctypes.c_double, _P, _SZ, _P,
+                              _P, _P, _P]),
+    "saf_frame_csr": (_I32, [_P, _I64, _I32, _I32, _I32, _I64, _I32, _I32, _P, _P, _P]),
+    "saf_bsa_fwd_frames": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _P, _I32, _I32, _I32,
+                                  _F32, _I32, _P]),
     "saf_bsa_pool_workspace_bytes": (_I64, [_I64, _I64, _I32]),
     "saf_bsa_fwd_pool": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _P, _I64, _I32, _I32, _F32, _I32, _I32, _P,
                                 _I64, _P, _P]),

@@ -16,7 +16,8 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
                       int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
-                      float* pool_rmax, float* pool_lse, cudaStream_t stream);
+                      const FrameMaskArgs* frames, float* pool_rmax, float* pool_lse,
+                      cudaStream_t stream);
 
 namespace {
 
@@ -265,7 +266,8 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int32_t block_m, int32_t block_n, const float* kv_bias,
                       int64_t kv_bias_stride_bh, float sm_scale, int32_t lead_rows,
-                      const int32_t* row_ranges, float* pool_rmax, float* pool_lse, void* stream) {
+                      const int32_t* row_ranges, const FrameMaskArgs* frames, float* pool_rmax,
+                      float* pool_lse, void* stream) {
   int32_t rc = check_tensor4(q);
   if (rc != SAF_OK) return rc;
   if ((rc = check_operand(k, q)) != SAF_OK) return rc;
@@ -279,6 +281,15 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   if (q->S > 0x7fffffff || k->S > 0x7fffffff || q->B * q->H > 65535) return SAF_ERR_SHAPE;
   if (row_ranges != nullptr && (reinterpret_cast<uintptr_t>(row_ranges) & 15) != 0) return SAF_ERR_STRIDE;
   if (row_ranges != nullptr && kv_bias != nullptr) return SAF_ERR_UNSUPPORTED;
+  if (frames != nullptr) {
+    if (row_ranges != nullptr || kv_bias != nullptr || pool_rmax != nullptr) return SAF_ERR_UNSUPPORTED;
+    if (frames->bits == nullptr) return SAF_ERR_ARG;
+    if (frames->frames < 1 || frames->frames > 32 || frames->text_len < 0 || frames->frame_len < block_n ||
+        q->S != k->S ||
+        q->S != frames->text_len + static_cast<int64_t>(frames->frames) * frames->frame_len)
+      return SAF_ERR_SHAPE;
+    if (q->dtype == SAF_F32) return SAF_ERR_UNSUPPORTED;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (q->dtype == SAF_F32) {
     if (pool_rmax != nullptr || pool_lse != nullptr) return SAF_ERR_UNSUPPORTED;
@@ -304,7 +315,7 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   return bsa_fwd_sm100(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                        kv_bias_stride_bh, sm_scale,
                        static_cast<int>(lead_tiles < 65535 ? lead_tiles : 65535), row_ranges,
-                       pool_rmax, pool_lse, st);
+                       frames, pool_rmax, pool_lse, st);
 }
 
 extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k,
@@ -315,7 +326,20 @@ extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k
                                       float sm_scale, int32_t lead_rows, const int32_t* row_ranges,
                                       void* stream) {
   return bsa_fwd_entry(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
-                       kv_bias_stride_bh, sm_scale, lead_rows, row_ranges, nullptr, nullptr, stream);
+                       kv_bias_stride_bh, sm_scale, lead_rows, row_ranges, nullptr, nullptr, nullptr,
+                       stream);
+}
+
+extern "C" int32_t saf_bsa_fwd_frames(const saf_tensor4* q, const saf_tensor4* k,
+                                      const saf_tensor4* v, const saf_tensor4* o,
+                                      const int32_t* row_ptr, const int32_t* col_idx,
+                                      int64_t col_capacity, int32_t block_m, int32_t block_n,
+                                      const uint32_t* frame_bits, int32_t text_len, int32_t frames,
+                                      int32_t frame_len, float sm_scale, int32_t lead_rows,
+                                      void* stream) {
+  const FrameMaskArgs fm{frame_bits, text_len, frame_len, frames};
+  return bsa_fwd_entry(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, nullptr, 0,
+                       sm_scale, lead_rows, nullptr, &fm, nullptr, nullptr, stream);
 }
 
 extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,

@@ -39,6 +39,9 @@ struct EnergyParams {
   int min_retain, max_retain, text_blocks;
   double* mass_out;  // nullable [rows, n]
   uint8_t* mask;     // [rows, n]
+  // 0: energy rule; 1: adaptive top-k from init_k (transfer_attn_to_mask
+  // mode "topk", SparseGen_Plus.py:28-50)
+  int mode, init_k;
 };
 
 __global__ void __launch_bounds__(32 * kEnergyWarps) energy_select_kernel(const EnergyParams p) {
@@ -89,20 +92,34 @@ __global__ void __launch_bounds__(32 * kEnergyWarps) energy_select_kernel(const 
   if (lane == 0) {
     // running sums in sorted order; total = the last running sum
     double cum = 0.0;
-    for (int r = 0; r < n; ++r) cum = __dadd_rn(cum, val[order[r]]);
-    const double target = __dmul_rn(p.threshold, cum);
-    double run = 0.0;
-    int k = n;
+    double at_k = 0.0;  // running sum of the first init_k (topk mode)
     for (int r = 0; r < n; ++r) {
-      run = __dadd_rn(run, val[order[r]]);
-      if (run >= target) {
-        k = r;
-        break;
-      }
+      cum = __dadd_rn(cum, val[order[r]]);
+      if (r == p.init_k - 1) at_k = cum;
     }
-    k = k < p.min_retain ? p.min_retain : k;
-    k = k > p.max_retain ? p.max_retain : k;
-    k = k > n ? n : k;
+    int k = n;
+    if (p.mode == 1) {
+      // grow the rows whose first init_k blocks hold under 60 % of the mass
+      // to 3x, then cut every row under 90 % to 2/3 of its count
+      k = p.init_k < n ? p.init_k : n;
+      const bool grow = !(at_k >= __dmul_rn(0.6, cum)) && k < n;
+      const bool cut = !(at_k >= __dmul_rn(0.9, cum)) && k < n;
+      if (grow) k = 3 * k < n ? 3 * k : n;
+      if (cut) k = (k / 3) * 2 < n ? (k / 3) * 2 : n;
+    } else {
+      const double target = __dmul_rn(p.threshold, cum);
+      double run = 0.0;
+      for (int r = 0; r < n; ++r) {
+        run = __dadd_rn(run, val[order[r]]);
+        if (run >= target) {
+          k = r;
+          break;
+        }
+      }
+      k = k < p.min_retain ? p.min_retain : k;
+      k = k > p.max_retain ? p.max_retain : k;
+      k = k > n ? n : k;
+    }
     for (int r = 0; r < k; ++r) keep[order[r]] = 1;
   }
   __syncwarp();
@@ -116,22 +133,23 @@ __global__ void __launch_bounds__(32 * kEnergyWarps) energy_select_kernel(const 
 
 using namespace saf;
 
-extern "C" int32_t saf_energy_select(const double* in, int32_t is_mass, int64_t BH, int32_t nbq,
-                                     int32_t nbk, int32_t block_n, int64_t Sk, double scale,
-                                     double threshold, int32_t min_retain, int32_t max_retain,
-                                     int32_t text_blocks, double* mass_out, uint8_t* mask,
-                                     void* stream) {
+namespace {
+int32_t select_entry(const double* in, int32_t is_mass, int64_t BH, int32_t nbq, int32_t nbk,
+                     int32_t block_n, int64_t Sk, double scale, double threshold, int32_t min_retain,
+                     int32_t max_retain, int32_t text_blocks, double* mass_out, uint8_t* mask, int mode,
+                     int32_t init_k, void* stream) {
   if (in == nullptr || mask == nullptr) return SAF_ERR_ARG;
   if (BH <= 0 || nbq <= 0 || nbk <= 0 || nbk > kEnergyMaxN) return SAF_ERR_SHAPE;
   if (!is_mass && (block_n <= 0 || Sk <= static_cast<int64_t>(nbk - 1) * block_n ||
                    Sk > static_cast<int64_t>(nbk) * block_n))
     return SAF_ERR_SHAPE;
   if (min_retain < 0 || max_retain < 0 || text_blocks < 0) return SAF_ERR_ARG;
+  if (mode == 1 && (init_k < 1 || init_k > nbk)) return SAF_ERR_ARG;
   int32_t rc;
   DeviceScope dev_scope;
   if ((rc = dev_scope.bind(in)) != SAF_OK) return rc;
   EnergyParams p{in, is_mass != 0, BH * nbq, nbq, nbk, block_n, static_cast<int>(Sk), scale, threshold,
-                 min_retain, max_retain, text_blocks, mass_out, mask};
+                 min_retain, max_retain, text_blocks, mass_out, mask, mode, mode == 1 ? init_k : 0};
   const int64_t rows = BH * nbq;
   const size_t smem = static_cast<size_t>(kEnergyWarps) * nbk * (8 + 4 + 1);
   if (smem > 48 * 1024)
@@ -141,4 +159,22 @@ extern "C" int32_t saf_energy_select(const double* in, int32_t is_mass, int64_t 
                          smem, static_cast<cudaStream_t>(stream)>>>(p);
   SAF_CUDA_TRY(cudaGetLastError());
   return SAF_OK;
+}
+}  // namespace
+
+extern "C" int32_t saf_energy_select(const double* in, int32_t is_mass, int64_t BH, int32_t nbq,
+                                     int32_t nbk, int32_t block_n, int64_t Sk, double scale,
+                                     double threshold, int32_t min_retain, int32_t max_retain,
+                                     int32_t text_blocks, double* mass_out, uint8_t* mask,
+                                     void* stream) {
+  return select_entry(in, is_mass, BH, nbq, nbk, block_n, Sk, scale, threshold, min_retain, max_retain,
+                      text_blocks, mass_out, mask, 0, 0, stream);
+}
+
+extern "C" int32_t saf_topk_adaptive_select(const double* in, int32_t is_mass, int64_t BH, int32_t nbq,
+                                            int32_t nbk, int32_t block_n, int64_t Sk, double scale,
+                                            int32_t init_k, int32_t text_blocks, double* mass_out,
+                                            uint8_t* mask, void* stream) {
+  return select_entry(in, is_mass, BH, nbq, nbk, block_n, Sk, scale, 0.0, 0, 0, text_blocks, mass_out,
+                      mask, 1, init_k, stream);
 }

@@ -18,7 +18,8 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int32_t block_m, int32_t block_n, const float* kv_bias,
                       int64_t kv_bias_stride_bh, float sm_scale, int32_t lead_rows,
-                      const int32_t* row_ranges, float* pool_rmax, float* pool_lse, void* stream);
+                      const int32_t* row_ranges, const saf::FrameMaskArgs* frames, float* pool_rmax,
+                      float* pool_lse, void* stream);
 
 namespace saf {
 namespace {
@@ -105,7 +106,7 @@ extern "C" int32_t saf_bsa_fwd_pool(const saf_tensor4* q, const saf_tensor4* k, 
       rmax, n_r, -INFINITY);
   SAF_CUDA_TRY(cudaGetLastError());
   rc = bsa_fwd_entry(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, nullptr, 0, sm_scale,
-                     lead_rows, nullptr, rmax, lse, stream);
+                     lead_rows, nullptr, nullptr, rmax, lse, stream);
   if (rc != SAF_OK) return rc;
   const int64_t warps1 = BH * nbk, warps2 = BH * nbp;
   pool_map_kernel<<<static_cast<unsigned>((warps1 + 7) / 8), 256, 0, st>>>(

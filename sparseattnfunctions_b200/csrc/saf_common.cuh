@@ -51,6 +51,15 @@ class DeviceScope {
 
 inline int elem_bytes(int32_t dtype) { return dtype == SAF_F32 ? 4 : 2; }
 
+// Per-head frame x frame masks over a [text | frames x frame_len] token
+// sequence: bits[g * frames + f1] has bit f2 set when video queries of frame
+// f1 of head g may see the video keys of frame f2 (text rows and text keys
+// are always visible).
+struct FrameMaskArgs {
+  const uint32_t* bits;
+  int32_t text_len, frame_len, frames;
+};
+
 // Common checks of a [B,H,S,D] view: non-null, D-stride 1 implied, positive
 // sizes, known dtype.
 inline int32_t check_tensor4(const saf_tensor4* t) {

@@ -170,6 +170,26 @@ def energy_select(x: torch.Tensor, *, threshold: float, min_retain: int, max_ret
     return (mask, mass) if return_mass else mask
 
 
+def topk_adaptive_select(x: torch.Tensor, *, init_k: int, text_blocks: int = 0, is_mass: bool = True,
+                         scale: float = 1.0, block_n: int = 0, Sk: int = 0) -> torch.Tensor:
+    """Adaptive top-k block mask from ``x [B, H, nbq, nbk]`` (the topk mode of
+    ``transfer_attn_to_mask``): start from ``init_k`` blocks per row, grow
+    rows under 60 % of the mass to 3x, then cut rows under 90 % to 2/3.
+    Returns the uint8 mask ``[B, H, nbq, nbk]``."""
+    dev = _require_cuda(x)
+    if x.dim() != 4:
+        raise ValueError("expected a [B, H, nbq, nbk] tensor")
+    x = x.to(torch.float64).contiguous()
+    B, H, nbq, nbk = x.shape
+    mask = torch.empty(B, H, nbq, nbk, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_topk_adaptive_select(x.data_ptr(), int(is_mass), B * H, nbq, nbk, int(block_n),
+                                                  int(Sk), float(scale), int(init_k), int(text_blocks), None,
+                                                  mask.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_topk_adaptive_select", rc)
+    return mask
+
+
 def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int, dense_rows: int = 0) -> BlockCSR:
     """Dense boolean block mask ``[B, H, nbq, nbk]`` -> ``BlockCSR``.  ``dense_rows``
     tells ``bsa_fwd`` how many leading row blocks have the longest lists."""
@@ -191,6 +211,90 @@ def mask_to_csr(block_mask: torch.Tensor, block_m: int, block_n: int, dense_rows
                                          row_ptr.data_ptr(), col_idx.data_ptr(), _stream_ptr(dev))
     _lib.check("saf_mask_to_csr", rc)
     return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n, dense_rows=dense_rows)
+
+
+@dataclass
+class FrameMask:
+    """Per-head frame x frame visibility of a [text | frames x frame_len]
+    sequence: ``bits`` int32 ``[B*H, frames]`` (bit f2 of word f1 set when
+    video queries of frame f1 see the video keys of frame f2), ``mask`` uint8
+    ``[B, H, frames, frames]`` and, when requested, the fp64 frame map."""
+
+    bits: torch.Tensor
+    mask: torch.Tensor
+    map: Optional[torch.Tensor]
+    text_len: int
+    frames: int
+    frame_len: int
+
+
+def frame_mask(q: torch.Tensor, k: torch.Tensor, spatial: torch.Tensor, *, text_len: int, frames: int,
+               frame_len: int, threshold: float = 0.9, sm_scale: float = 0.125,
+               return_map: bool = False) -> FrameMask:
+    """Frame-scope mask from the tokens sampled at every text position and at
+    the ``spatial`` positions (int, in ``[0, frame_len)``) of every frame:
+    the frame x frame attention map and the per-head energy rule of
+    ``generate_attention_mask_frame_scope`` (saf_frame_mask)."""
+    dev = _require_cuda(q, k)
+    q, k = _d_last(q), _d_last(k)
+    B, H, S, D = q.shape
+    sp = spatial.to(device=dev, dtype=torch.int32).contiguous().reshape(-1)
+    n = sp.numel()
+    lib = _lib.load()
+    ws_bytes = int(lib.saf_frame_mask_workspace_bytes(B * H, frames, n, text_len, D))
+    ws = torch.empty(max(ws_bytes, 8), dtype=torch.uint8, device=dev)
+    bits = torch.empty(B * H, frames, dtype=torch.int32, device=dev)
+    mask = torch.empty(B, H, frames, frames, dtype=torch.uint8, device=dev)
+    fmap = torch.empty(B, H, frames, frames, dtype=torch.float64, device=dev) if return_map else None
+    tq, tk = _t4(q), _t4(k)
+    with torch.cuda.device(dev):
+        rc = lib.saf_frame_mask(ctypes.byref(tq), ctypes.byref(tk), sp.data_ptr(), n, text_len, frames,
+                                frame_len, float(sm_scale), float(threshold), ws.data_ptr(), ws.numel(),
+                                fmap.data_ptr() if fmap is not None else None, mask.data_ptr(),
+                                bits.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_frame_mask", rc)
+    return FrameMask(bits, mask, fmap, text_len, frames, frame_len)
+
+
+def frame_csr(fm: FrameMask, B: int, H: int, block_m: int = 128, block_n: int = 128) -> BlockCSR:
+    """The key blocks each query block can touch under ``fm`` (saf_frame_csr)."""
+    dev = _require_cuda(fm.bits)
+    S = fm.text_len + fm.frames * fm.frame_len
+    nbq, nbk = math.ceil(S / block_m), math.ceil(S / block_n)
+    row_ptr = torch.empty(B * H, nbq + 1, dtype=torch.int32, device=dev)
+    col_idx = torch.empty(B * H * nbq * nbk, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_frame_csr(fm.bits.data_ptr(), B * H, fm.text_len, fm.frames, fm.frame_len, S,
+                                       block_m, block_n, row_ptr.data_ptr(), col_idx.data_ptr(),
+                                       _stream_ptr(dev))
+    _lib.check("saf_frame_csr", rc)
+    text_rows = min(nbq, math.ceil(fm.text_len / block_m))
+    return BlockCSR(row_ptr, col_idx, B, H, nbq, nbk, block_m, block_n, dense_rows=text_rows)
+
+
+def bsa_fwd_frames(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, fm: FrameMask,
+                   sm_scale: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Block-sparse attention under the frame masks ``fm``: every visited
+    block is masked to the keys the query row's frame may see
+    (saf_bsa_fwd_frames)."""
+    dev = _require_cuda(q, k, v, fm.bits)
+    q, k, v = _d_last(q), _d_last(k), _d_last(v)
+    B, H, Sq, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} must match")
+    if (csr.B, csr.H) != (B, H):
+        raise ValueError("block list does not match q/k shapes")
+    if out is None:
+        out = torch.empty_like(q)
+    tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_bsa_fwd_frames(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(to),
+                                            csr.row_ptr.data_ptr(), csr.col_idx.data_ptr(), csr.col_idx.numel(),
+                                            csr.block_m, csr.block_n, fm.bits.data_ptr(), fm.text_len,
+                                            fm.frames, fm.frame_len, float(sm_scale), int(csr.dense_rows),
+                                            _stream_ptr(dev))
+    _lib.check("saf_bsa_fwd_frames", rc)
+    return out
 
 
 def bsa_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, csr: BlockCSR, sm_scale: float,

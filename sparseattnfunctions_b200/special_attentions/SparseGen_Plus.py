@@ -36,10 +36,23 @@ def transfer_attn_to_mask(attn: torch.Tensor, mode: str = "energy", init_k=None,
                           min_retain_ratio: float = 0.1, energy_threshold: float = 0.95,
                           text_blocks: int = 4) -> torch.Tensor:
     """Bool block mask ``[B, H, n, n']`` from a non-negative block attention
-    estimate ``attn`` (SparseGen_Plus.py:12-84, ``mode="energy"``)."""
-    if mode != "energy":
-        raise NotImplementedError(f"mode {mode!r}: only the energy mode is provided")
+    estimate ``attn`` (SparseGen_Plus.py:12-84).  ``mode="energy"``: per row
+    the smallest set of blocks holding ``energy_threshold`` of the mass,
+    clamped to the retain ratios.  ``mode="topk"``: ``init_k`` blocks per row
+    (a fraction of the row when below 1), tripled for rows whose first
+    ``init_k`` hold under 60 % of the mass, then cut to 2/3 for rows under
+    90 % (the reference's rule, :28-50).  Text rows / columns forced."""
     n = attn.shape[-1]
+    if mode == "topk":
+        if init_k is None:
+            raise ValueError("the topk mode needs an initial k (init_k)")
+        if attn.shape[-2] != n:
+            raise ValueError("the topk mode takes a square block map (the reference caps k at its row count)")
+        k0 = int(n * init_k) if init_k < 1 else int(init_k)
+        mask = kernels.topk_adaptive_select(attn, init_k=k0, text_blocks=text_blocks, is_mass=True)
+        return mask.bool()
+    if mode != "energy":
+        raise ValueError(f"Unsupported mode: {mode}")
     min_retain = max(1, int(n * min_retain_ratio))
     max_retain = max(1, int(n * max_retain_ratio))
     mask = kernels.energy_select(attn, threshold=energy_threshold, min_retain=min_retain,

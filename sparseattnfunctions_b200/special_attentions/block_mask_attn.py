@@ -8,10 +8,17 @@ selects blocks by mean-pooled scores (top ``density`` of the key blocks of
 every row block, text rows / columns dense) and runs the sm_100a sparse
 attention kernel over the live blocks only, returning the output.
 
-``forward_backup`` keeps the reference's frame-scope idea (a frame x frame
-energy mask of the sampled attention map) but builds the block list directly
-on the unpadded sequence, so no token is padded or truncated
-(the reference pads Q and randomly truncates K/V: mask_related.py:87-167).
+``forward_backup`` is the reference's frame-scope path: a frame x frame
+mask from the attention of a sampled token subset (the per-head energy rule
+of generate_attention_mask_frame_scope, mask_related.py:194-245), then
+sparse attention where a video query of frame f1 sees the text keys and the
+keys of the frames f2 its head's mask allows.  The reference pads q to
+64-multiples per frame, randomly truncates k / v (mask_related.py:87-167)
+and expands the frame mask by an inner per-frame block mask computed with
+threshold 1 (which keeps every block in exact arithmetic); here the frame
+mask applies token by token on the unpadded sequence (saf_frame_csr lists
+the blocks, saf_bsa_fwd_frames masks inside them), so no token is padded,
+dropped or assigned to the wrong frame.
 """
 from __future__ import annotations
 
@@ -39,6 +46,7 @@ class BlockSparseAttention:
         self.text_dense = text_dense
         self.sm_scale = sm_scale
         self.last_csr = None  # block list of the latest call (for inspection)
+        self.last_frame_mask = None  # frame masks of the latest forward_backup call
 
     def select(self, q: torch.Tensor, k: torch.Tensor) -> kernels.BlockCSR:
         bs = self.block_size
@@ -55,6 +63,34 @@ class BlockSparseAttention:
         csr = self.select(q, k)
         self.last_csr = csr
         out = kernels.bsa_fwd(q, k, v, csr, scale, out=out)
+        if self.check_status:
+            _lib.raise_on_device_status(q.device.index)
+        return out
+
+    def forward_backup(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                       spatial: torch.Tensor | None = None, sample_num: int = 60,
+                       threshold: float = 0.9, scale_factor: float = 1 / 8,
+                       generator: torch.Generator | None = None) -> torch.Tensor:
+        """Frame-scope sparse attention (block_mask_attn.py:11-20).
+
+        ``spatial``: the ``sample_num`` positions inside a frame sampled in
+        every frame; drawn like the reference (``torch.randint`` on the CPU,
+        from ``generator`` or the default generator) when not given.
+        ``threshold`` / ``scale_factor``: the frame mask's energy fraction and
+        logit scale (the reference's base_threshold 0.9 and 1/8)."""
+        geo = self.geometry
+        B, H, S, D = q.shape
+        if S != geo.seq_len:
+            raise ValueError(f"sequence length {S} does not match the geometry's {geo.seq_len}")
+        if spatial is None:
+            spatial = torch.randint(0, geo.frame_len, (sample_num,), generator=generator)
+        fm = kernels.frame_mask(q, k, spatial, text_len=geo.text_len, frames=geo.frames,
+                                frame_len=geo.frame_len, threshold=threshold, sm_scale=scale_factor)
+        csr = kernels.frame_csr(fm, B, H, self.block_size, self.block_size)
+        self.last_frame_mask = fm
+        self.last_csr = csr
+        scale = self.sm_scale if self.sm_scale is not None else 1.0 / math.sqrt(D)
+        out = kernels.bsa_fwd_frames(q, k, v, csr, fm, scale)
         if self.check_status:
             _lib.raise_on_device_status(q.device.index)
         return out

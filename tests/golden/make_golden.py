@@ -15,6 +15,7 @@ the reference's outputs.
 Fixtures
   topk_masks.npz    get_sparse_attn_mask_from_topk (block_sparse_attn_kernel.py:31-39)
   energy_masks.npz  transfer_attn_to_mask(mode="energy") (SparseGen_Plus.py:12-84)
+  topk_adaptive_masks.npz  transfer_attn_to_mask(mode="topk") (SparseGen_Plus.py:28-50)
   tome_*.npz        bipartite_soft_matching_video + merge / unmerge
                     (utils/merge_unmerge.py:34-154), fp64 metric
   sta_layout.npz    SildingTileAttention's tile-window mask_mod (small and
@@ -32,6 +33,11 @@ Fixtures
                     fp64 on the KAT shapes, a ragged case with an empty row
                     and the config-1 shape; stored as per-row sums and a
                     fixed random projection of each output row
+  frame_scope.npz   generate_attention_mask_frame_scope (utils/mask_related.py:
+                    194-245) on seeded fp64 q / k: the spatial sample it
+                    drew (torch's CPU generator seeded before the call) and
+                    the frame x frame mask it returned, at a small geometry
+                    and at CogVideoX-2B's, for two thresholds
 """
 from __future__ import annotations
 
@@ -239,6 +245,47 @@ def attention_kat(root: str, bsk):
     return out
 
 
+# (name, seed, B, H, text, frames, height, width, sample_num, threshold)
+FRAME_CASES = [("small_t90", 401, 1, 2, 20, 5, 6, 8, 10, 0.9),
+               ("small_t70", 402, 2, 2, 20, 5, 6, 8, 10, 0.7),
+               ("cogvideox_t90", 403, 1, 2, 226, 13, 30, 45, 60, 0.9)]
+
+
+def frame_inputs(seed, B, H, text, frames, height, width):
+    """fp64 q, k [B, H, text + frames*height*width, 64]: a random vector per
+    (head, frame) shared by its tokens plus N(0, 1) noise (text: noise only),
+    so that frames attend to one another unevenly."""
+    rs = np.random.RandomState(seed)
+    fl = height * width
+    out = []
+    for _ in range(2):
+        centre = rs.randn(B, H, frames, 1, 64) * 1.5
+        vid = (centre + rs.randn(B, H, frames, fl, 64)).reshape(B, H, frames * fl, 64)
+        out.append(np.concatenate([rs.randn(B, H, text, 64), vid], axis=2))
+    return out[0], out[1]
+
+
+def frame_scope(root: str):
+    import torch
+
+    sys.path.insert(0, root)
+    from special_attentions.utils import mask_related as mr
+
+    out = {"cases": np.array([c[1:9] for c in FRAME_CASES], dtype=np.int64),
+           "thresholds": np.array([c[9] for c in FRAME_CASES])}
+    for name, seed, B, H, text, frames, height, width, n, thr in FRAME_CASES:
+        q, k = frame_inputs(seed, B, H, text, frames, height, width)
+        torch.manual_seed(seed)
+        spatial = torch.randint(0, width * height, (n,))
+        torch.manual_seed(seed)
+        mask = mr.generate_attention_mask_frame_scope(
+            torch.from_numpy(q), torch.from_numpy(k), text_length=text, f=frames, width=width,
+            height=height, sample_num=n, scale_factor=1 / 8, base_threshold=thr)
+        out[f"{name}_spatial"] = spatial.numpy().astype(np.int32)
+        out[f"{name}_mask"] = mask.numpy()
+    return out
+
+
 def closure_vars(fn):
     return {name: cell.cell_contents for name, cell in zip(fn.__code__.co_freevars, fn.__closure__)}
 
@@ -252,6 +299,15 @@ TOME_CASES = [  # (name, metric seed, C, r, generator seed or None)
 GEOM = dict(w=45, h=30, t=13, sx=3, sy=3, st=4)
 TEXT = 226
 PROJ_C = 240  # channel count that lets the reference's unmerge reshape to (2, 30, -1, 64)
+
+
+# (seed, B, H, n, init_k, power): inputs rand ** power, from flat to peaked rows
+TOPK_ADAPTIVE_CASES = [(501, 1, 2, 40, 0.1, 3.0), (502, 2, 2, 139, 0.1, 8.0), (503, 1, 3, 139, 5, 1.0),
+                       (504, 1, 2, 64, 0.25, 12.0)]
+
+
+def topk_adaptive_input(seed, B, H, n, power):
+    return np.random.RandomState(seed).rand(B, H, n, n) ** power
 
 
 def topk_input(seed, B, H, n):
@@ -292,6 +348,12 @@ def main(root: str):
             a, mode="energy", max_retain_ratio=mx, min_retain_ratio=mn, energy_threshold=thr).numpy()
     np.savez_compressed(HERE / "energy_masks.npz", cases=np.array(ENERGY_CASES), **masks)
 
+    masks = {}
+    for seed, B, H, n, init_k, power in TOPK_ADAPTIVE_CASES:
+        a = torch.from_numpy(topk_adaptive_input(seed, B, H, n, power))
+        masks[f"case_{seed}"] = sgp.transfer_attn_to_mask(a, mode="topk", init_k=init_k).numpy()
+    np.savez_compressed(HERE / "topk_adaptive_masks.npz", cases=np.array(TOPK_ADAPTIVE_CASES), **masks)
+
     for name, seed, C, r, gseed in TOME_CASES:
         metric = torch.from_numpy(tome_metric(seed, C))
         gen = None if gseed is None else torch.Generator().manual_seed(gseed)
@@ -327,6 +389,7 @@ def main(root: str):
         out["unmerge_proj"] = (un @ proj).reshape(-1).numpy()
         np.savez_compressed(HERE / f"{name}.npz", **out)
     np.savez_compressed(HERE / "attention_kat.npz", **attention_kat(root, bsk))
+    np.savez_compressed(HERE / "frame_scope.npz", **frame_scope(root))
     np.savez_compressed(HERE / "smart_layout.npz", **smart_layout(root))
     np.savez_compressed(HERE / "sta_layout.npz", **sta_layout(root))
     print("fixtures written to", HERE)

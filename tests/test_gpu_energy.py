@@ -103,3 +103,23 @@ def test_sparsegen_plus_warmup_pooling(cuda_device):
     assert np.array_equal(mask, ref_mask)
     ref = oatt.block_sparse_attention(q, k, v, mask, 1 / 8, 64, 64)
     assert np.abs(out.double().cpu().numpy() - ref).max() <= 2e-2
+
+
+def test_topk_mode_matches_reference_outputs(cuda_device):
+    """transfer_attn_to_mask(mode="topk") on the GPU against the reference's
+    own masks (tests/golden/topk_adaptive_masks.npz): bit-exact."""
+    import importlib.util
+    from pathlib import Path
+
+    from sparseattnfunctions_b200.special_attentions.SparseGen_Plus import transfer_attn_to_mask
+
+    golden = Path(__file__).resolve().parent / "golden"
+    spec = importlib.util.spec_from_file_location("make_golden", golden / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    data = np.load(golden / "topk_adaptive_masks.npz")
+    for seed, B, H, n, init_k, power in data["cases"]:
+        a = torch.from_numpy(mg.topk_adaptive_input(int(seed), int(B), int(H), int(n), float(power)))
+        init = float(init_k) if init_k < 1 else int(init_k)
+        got = transfer_attn_to_mask(a.to(cuda_device), mode="topk", init_k=init)
+        assert np.array_equal(got.cpu().numpy(), data[f"case_{int(seed)}"]), f"case {int(seed)}"

@@ -112,8 +112,10 @@ def test_processor_status_check_raises_on_timeout(cuda_device):
     from sparseattnfunctions_b200 import workloads
 
     assert _lib.read_device_status(0, clear=True) == 0
-    geo = VideoGeometry(226, 4, 16, 24)
-    q, k, v = (t.to(cuda_device) for t in workloads.video_qkv(geo, B=2, H=4, seed=5))
+    # large enough that every CTA takes several tiles and some wait does not
+    # complete at its first poll
+    geo = VideoGeometry(226, 8, 30, 45)
+    q, k, v = (t.to(cuda_device) for t in workloads.video_qkv(geo, B=2, H=8, seed=5))
     proc = BlockSparseAttention(block_size=128, density=0.3, geometry=geo, check_status=True)
     good = proc(q, k, v)
     old = _lib.get_wait_budget_ns()

@@ -108,12 +108,9 @@ struct BsaParams {
 // merged and every tile carries a 2-bit row mask: bit 0 = rows [0,64) live,
 // bit 1 = rows [64,128) live.  Every role of the CTA runs its own copy, so
 // all of them see the same sequence.  Out-of-range columns are skipped.
-// The next column of each list is loaded one step ahead, so its global-load
-// latency overlaps the current block's work.
 struct TileIter {
   const int32_t* cols;
   int32_t p0, e0, p1, e1;  // CSR offsets are int32 by contract
-  int32_t n0, n1;          // cols[p0] / cols[p1] when p0 < e0 / p1 < e1
   int nbk;
   bool two_rows;
   unsigned int* status;
@@ -135,8 +132,6 @@ struct TileIter {
       p1 = clampi(rp[r0 + 1]);
       e1 = clampi(rp[r0 + 2]);
     }
-    n0 = p0 < e0 ? cols[p0] : 0;
-    n1 = p1 < e1 ? cols[p1] : 0;
   }
   __device__ bool valid(int c) {
     if (c >= 0 && c < nbk) return true;
@@ -150,28 +145,24 @@ struct TileIter {
       int c;
       uint32_t m;
       if (!two_rows) {
-        c = n0;
+        c = cols[p0++];
         m = 3u;
-        if (++p0 < e0) n0 = cols[p0];
       } else {
-        const int c0 = h0 ? n0 : 0x7fffffff;
-        const int c1 = h1 ? n1 : 0x7fffffff;
-        bool adv0 = false, adv1 = false;
+        const int c0 = h0 ? cols[p0] : 0x7fffffff;
+        const int c1 = h1 ? cols[p1] : 0x7fffffff;
         if (c0 <= c1) {
           c = c0;
           m = 1u;
-          adv0 = true;
+          ++p0;
           if (c1 == c0) {
             m |= 2u;
-            adv1 = true;
+            ++p1;
           }
         } else {
           c = c1;
           m = 2u;
-          adv1 = true;
+          ++p1;
         }
-        if (adv0 && ++p0 < e0) n0 = cols[p0];
-        if (adv1 && ++p1 < e1) n1 = cols[p1];
       }
       if (valid(c)) {
         col = c;
@@ -235,10 +226,9 @@ struct Layout {
   static constexpr int kOffOnes = kOffBias + (kBias ? kVS * kBiasTile : 0);  // ones column
   static constexpr int kOffBar = kOffOnes + (kBias ? kBM * 32 : 0);
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           b_full[VS], s_full, s_empty, p_full[0], pv_full[0], drain,
-  //           b_empty[VS], q_empty, tile_full[2], tile_empty[2], p_full[1],
-  //           pv_full[1]  (p_full / pv_full per half of the block's keys)
-  static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 12;
+  //           b_full[VS], s_full, s_empty, p_full, pv_full, drain, b_empty[VS],
+  //           q_empty, tile_full[2], tile_empty[2]
+  static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 10;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
@@ -294,14 +284,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto bar_b_empty = [&](int s) { return bar0 + 8u * (1 + 2 * kKS + 3 * kVS + 5 + s); };
   const uint32_t bar_s_full = bar0 + 8u * (1 + 2 * kKS + 3 * kVS);
   const uint32_t bar_s_empty = bar_s_full + 8;
+  const uint32_t bar_p_full = bar_s_full + 16;
+  const uint32_t bar_pv_full = bar_s_full + 24;
   const uint32_t bar_drain = bar_s_full + 32;
   const uint32_t bar_q_empty = bar0 + 8u * (1 + 2 * kKS + 4 * kVS + 5);
   auto bar_tile_full = [&](int s) { return bar_q_empty + 8u * (1 + s); };
   auto bar_tile_empty = [&](int s) { return bar_q_empty + 8u * (3 + s); };
-  // P of keys [0, BN/2) / [BN/2, BN) stored (softmax -> MMA); O += P V of
-  // that half done (MMA -> softmax)
-  auto bar_p_full = [&](int h) { return h == 0 ? bar_s_full + 16 : bar_q_empty + 8u * 5; };
-  auto bar_pv_full = [&](int h) { return h == 0 ? bar_s_full + 24 : bar_q_empty + 8u * 6; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   volatile int* tile_slot = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);  // [2]
@@ -320,10 +308,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     mbar_init(bar_s_full, 1);
     mbar_init(bar_s_empty, 128);  // the softmax threads
-    for (int h = 0; h < 2; ++h) {
-      mbar_init(bar_p_full(h), 128);
-      mbar_init(bar_pv_full(h), 1);
-    }
+    mbar_init(bar_p_full, 128);
+    mbar_init(bar_pv_full, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_q_empty, 1);
     for (int s = 0; s < 2; ++s) {
@@ -461,26 +447,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t kIdescPV = idesc_f16(kBM, kD, kBF16, false, true);
       const uint32_t tS = tmem + kColS, tO = tmem + kColO, tP = tmem + kColP;
 
-      // O += P V for global block jg, in two halves of the block's keys as
-      // the softmax publishes them; `first` starts the tile's accumulator.
+      // O += P V for global block jg; `first` starts the tile's accumulator.
       auto issue_pv = [&](int jg, bool first) -> bool {
         const int sv = jg % kVS;
         const uint32_t pv = (jg / kVS) & 1;
         if (!mbar_wait(bar_v_full(sv), pv, abort_flag, p.status, p.budget_ns)) return false;
+        if (!mbar_wait(bar_p_full, jg & 1, abort_flag, p.status, p.budget_ns)) return false;
+        tc_fence_after();
         const uint32_t vbase = sV0 + sv * L::kKVBytes;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(bar_p_full(h), jg & 1, abort_flag, p.status, p.budget_ns)) return false;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = h * (BN / 32); kk < (h + 1) * (BN / 32); ++kk) {
-            // B = V^T: N = D (contiguous, one 128B swizzle atom), K = kv rows;
-            // 16 kv rows = two 8-row atoms = 2048 bytes.
-            const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, L::kKVBytes, 1024);
-            tc_mma_ts(tO, tP + kk * 8, bdesc, kIdescPV, (!first || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(bar_pv_full(h));
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          // B = V^T: N = D (contiguous, one 128B swizzle atom), K = kv rows;
+          // 16 kv rows = two 8-row atoms = 2048 bytes.
+          const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, L::kKVBytes, 1024);
+          tc_mma_ts(tO, tP + kk * 8, bdesc, kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
+        tc_commit(bar_pv_full);
         tc_commit(bar_v_empty(sv));
         return true;
       };
@@ -676,142 +658,120 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (!(live && e < valid)) t[e] = -INFINITY;
         }
       }
-      // The online softmax runs per half of the block (BN / 2 keys): the MMA
-      // warp starts O += P V of a half as soon as that half of P is stored,
-      // and the next block's half of P waits only for the product of the same
-      // half.  Under lazy rescaling the running max rarely moves, so P is
-      // computed speculatively with the current running max while the half's
-      // max is accumulated alongside (ALU work next to the MUFU work); only
-      // if the row's max jumped past the threshold does the warp recompute the
-      // half's P (the scores are still in registers) and rescale O.  A warp
-      // with a row that has not seen a live score yet takes the max-first
-      // order.
-      constexpr int HC = NC / 2;  // 32-column chunks per half
-      float mx_block = -INFINITY;
-      bool stop = false;
+      // Under lazy rescaling the running max rarely moves, so P is computed
+      // speculatively with the current running max while the block max is
+      // accumulated alongside (ALU work next to the MUFU work); only if the
+      // row's max jumped past the threshold does the warp recompute P (the
+      // scores are still in registers) and rescale O.  A warp with a row that
+      // has not seen a live score yet takes the max-first order.
+      const bool spec = __all_sync(0xffffffffu, m_run != -INFINITY);
+      bool pv_done = (j == 0);
+      // PV of the previous block must be done before P is overwritten and
+      // before O is rescaled.
+      auto wait_pv = [&]() -> bool {
+        if (pv_done) return true;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_pv_full, (jg - 1) & 1, abort_flag, p.status,
+                                                p.budget_ns)))
+          return false;
+        tc_fence_after();
+        pv_done = true;
+        return true;
+      };
+      f2 rs = mk2(0.f, 0.f);
+      float mx = -INFINITY;
+      // P = exp2(logit - m) in the input type, row sum in fp32 pairs, 32
+      // scores at a time (the empty asm after each store keeps the next part's
+      // exp2 from being scheduled early, bounding live registers).
+      // keep: 0 zeroes P of a row with no live score yet (the polynomial maps
+      // -inf to 2^-126, not 0), keeping such rows at l = 0 as the reference.
+      auto exp_pass = [&](float neg_m, bool with_max, float keep) -> bool {
+        const f2 negm2 = mk2(neg_m, neg_m);
+        const f2 keep2 = mk2(keep, keep);
+        rs = mk2(0.f, 0.f);
+        float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const bool spec = __all_sync(0xffffffffu, m_run != -INFINITY);
-        bool pv_done = (j == 0);
-        // the previous block's product of this half must be done before this
-        // half of P is overwritten
-        auto wait_pv = [&]() -> bool {
-          if (pv_done) return true;
-          if (!__all_sync(0xffffffffu, mbar_wait(bar_pv_full(hh), (jg - 1) & 1, abort_flag, p.status,
-                                                  p.budget_ns)))
-            return false;
-          tc_fence_after();
-          pv_done = true;
-          return true;
-        };
-        f2 rs = mk2(0.f, 0.f);
-        float mx = -INFINITY;
-        // P = exp2(logit - m) in the input type, row sum in fp32 pairs, 32
-        // scores at a time (the empty asm after each store keeps the next
-        // part's exp2 from being scheduled early, bounding live registers).
-        // keep: 0 zeroes P of a row with no live score yet (the polynomial
-        // maps -inf to 2^-126, not 0), keeping such rows at l = 0.
-        auto exp_pass = [&](float neg_m, bool with_max, float keep) -> bool {
-          const f2 negm2 = mk2(neg_m, neg_m);
-          const f2 keep2 = mk2(keep, keep);
-          rs = mk2(0.f, 0.f);
-          float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        for (int c = 0; c < NC; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int c = hh * HC; c < (hh + 1) * HC; ++c) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              if (with_max)
-                acc[e & 3] = fmax3(acc[e & 3], t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
-              f2 x = mk2(t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
-              x = fma2(x, sl2x2, negm2);
-              float e0, e1;
-              if (exp2_on_fma(e)) {
-                const f2 y = exp2_poly2(x);
-                e0 = lo2(y);
-                e1 = hi2(y);
-              } else {
-                e0 = ex2_approx(lo2(x));
-                e1 = ex2_approx(hi2(x));
-              }
-              if (!with_max) {
-                const f2 z = mul2(mk2(e0, e1), keep2);
-                e0 = lo2(z);
-                e1 = hi2(z);
-              }
-              rs = add2(rs, mk2(e0, e1));
-              pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
+          for (int e = 0; e < 16; ++e) {
+            if (with_max)
+              acc[e & 3] = fmax3(acc[e & 3], t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
+            f2 x = mk2(t[c * 32 + 2 * e], t[c * 32 + 2 * e + 1]);
+            x = fma2(x, sl2x2, negm2);
+            float e0, e1;
+            if (exp2_on_fma(e)) {
+              const f2 y = exp2_poly2(x);
+              e0 = lo2(y);
+              e1 = hi2(y);
+            } else {
+              e0 = ex2_approx(lo2(x));
+              e1 = ex2_approx(hi2(x));
             }
-            if (c == hh * HC && !wait_pv()) return false;
-            tmem_st16(tP + c * 16, pk);
-            if (c + 1 < (hh + 1) * HC) {
-              asm volatile("" : "+l"(rs.v));
-#pragma unroll
-              for (int e = 0; e < 32; ++e) asm volatile("" : "+f"(t[(c + 1) * 32 + e]));
+            if (!with_max) {
+              const f2 z = mul2(mk2(e0, e1), keep2);
+              e0 = lo2(z);
+              e1 = hi2(z);
             }
+            rs = add2(rs, mk2(e0, e1));
+            pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
           }
-          if (with_max) mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
-          return true;
-        };
+          if (c == 0 && !wait_pv()) return false;
+          tmem_st16(tP + c * 16, pk);
+          if (c + 1 < NC) {
+            asm volatile("" : "+l"(rs.v));
+#pragma unroll
+            for (int e = 0; e < 32; ++e) asm volatile("" : "+f"(t[(c + 1) * 32 + e]));
+          }
+        }
+        if (with_max) mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
+        return true;
+      };
 
-        if (spec) {
-          if (!exp_pass(-m_run, true, 1.f)) {
-            stop = true;
-            break;
-          }
-        } else {
-          float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-          for (int i = hh * BN / 4; i < (hh + 1) * BN / 4; ++i)
-            acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
-          mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
+      if (spec) {
+        if (!exp_pass(-m_run, true, 1.f)) {
+          ok = false;
+          break;
         }
-        mx *= sl2;
-        mx_block = fmaxf(mx_block, mx);
-        const bool upd = mx > m_run + kRescaleThreshold;
-        const float m_new = upd ? mx : m_run;
-        const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
-        const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
-        const bool any_upd = __any_sync(0xffffffffu, upd);
-        if (!spec || any_upd) {
-          if (!exp_pass(neg_m, false, m_new == -INFINITY ? 0.f : 1.f)) {
-            stop = true;
-            break;
-          }
-        }
-        // O holds the products of the earlier blocks (j > 0) and, for the
-        // second half, of this block's first half: rescale it once they are
-        // done (products complete in issue order).
-        if (any_upd && (j > 0 || hh == 1)) {
-          const uint32_t bar = hh == 0 ? bar_pv_full(1) : bar_pv_full(0);
-          const uint32_t par = hh == 0 ? static_cast<uint32_t>((jg - 1) & 1) : static_cast<uint32_t>(jg & 1);
-          if (!__all_sync(0xffffffffu, mbar_wait(bar, par, abort_flag, p.status, p.budget_ns))) {
-            stop = true;
-            break;
-          }
-          tc_fence_after();
+      } else {
+        float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int c = 0; c < kD / 32; ++c) {
-            uint32_t orr[32];
-            tmem_ld32(tO + 32 * c, orr);
-            tmem_wait_ld(orr);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-            tmem_st32(tO + 32 * c, orr);
-          }
-        }
-        l_run = l_run * alpha + (lo2(rs) + hi2(rs));
-        m_run = m_new;
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar_p_full(hh));
+        for (int i = 0; i < BN / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
+        mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
       }
-      if (stop) {
-        ok = false;
-        break;
-      }
+      mx *= sl2;
       if (p.pool_rmax != nullptr && q0 + row < p.Sq)
-        p.pool_rmax[(static_cast<int64_t>(g) * p.nbk + col) * p.Sq + q0 + row] = mx_block;
+        p.pool_rmax[(static_cast<int64_t>(g) * p.nbk + col) * p.Sq + q0 + row] = mx;
+      const bool upd = mx > m_run + kRescaleThreshold;
+      const float m_new = upd ? mx : m_run;
+      const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
+      const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
+      const bool any_upd = __any_sync(0xffffffffu, upd);
+      if (!spec || any_upd) {
+        if (!exp_pass(neg_m, false, m_new == -INFINITY ? 0.f : 1.f)) {
+          ok = false;
+          break;
+        }
+      }
+      if (j > 0 && any_upd) {
+        if (!wait_pv()) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t orr[32];
+          tmem_ld32(tO + 32 * c, orr);
+          tmem_wait_ld(orr);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+          tmem_st32(tO + 32 * c, orr);
+        }
+      }
+      l_run = l_run * alpha + (lo2(rs) + hi2(rs));
+      m_run = m_new;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_p_full);
       ++j;
     }
 
@@ -822,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool have_o =
         ok && j > 0 &&
         __all_sync(0xffffffffu,
-                   mbar_wait(bar_pv_full(1), (jbase + j - 1) & 1, abort_flag, p.status, p.budget_ns));
+                   mbar_wait(bar_pv_full, (jbase + j - 1) & 1, abort_flag, p.status, p.budget_ns));
     if (have_o) tc_fence_after();
     const int qrow = q0 + row;
     const float inv_l = 1.f / l_run;

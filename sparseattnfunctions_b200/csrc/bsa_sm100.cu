@@ -203,9 +203,11 @@ __device__ __forceinline__ f2 exp2_poly2(f2 x) {
 }
 
 // Pairs e of every 16-pair chunk whose exp2 runs on the FMA pipe (bit e of
-// the mask); the others use the MUFU.
+// the mask); the others use the MUFU.  Two pairs of 16 (12.5 %, pairs 7 and
+// 15) measured 2.5 % faster at CogVideoX-2B config 2 (0.915 against 0.938
+// ms); four (25 %) no faster, eight (50 %) 10 % slower.
 #ifndef SAF_EXP2_FMA_MASK
-#define SAF_EXP2_FMA_MASK 0x0000u  // measured slower when the kernel is not MUFU-bound
+#define SAF_EXP2_FMA_MASK 0x8080u
 #endif
 __host__ __device__ constexpr bool exp2_on_fma(int e) { return (SAF_EXP2_FMA_MASK >> e) & 1u; }
 
@@ -883,6 +885,14 @@ int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
   auto kern = bsa_fwd_sm100_kernel<BN, kBias, kBF16, kMask>;
   const int smem = Layout<BN, kBias>::kDynSmem;
   SAF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  // setmaxnreg.inc only draws on the registers the CTA was launched with: a
+  // build that launched with fewer than the split needs would wait forever
+  static const int launch_regs = [] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, bsa_fwd_sm100_kernel<BN, kBias, kBF16, kMask>) == cudaSuccess ? fa.numRegs
+                                                                                                  : 0;
+  }();
+  if (launch_regs * kThreads < 128 * static_cast<int>(kRegsCtl + kRegsSoftmax)) return SAF_ERR_UNSUPPORTED;
   int dev = 0, sms = 0;
   SAF_CUDA_TRY(cudaGetDevice(&dev));
   SAF_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

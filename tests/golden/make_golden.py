@@ -38,6 +38,9 @@ Fixtures
                     drew (torch's CPU generator seeded before the call) and
                     the frame x frame mask it returned, at a small geometry
                     and at CogVideoX-2B's, for two thresholds
+  mask_layout.npz   get_block_mask (utils/mask_related.py:397-404) on seeded
+                    masks, and the query side of preprocess_qkv /
+                    reverse_process_out (:87-187) on a token-index tensor
 """
 from __future__ import annotations
 
@@ -265,6 +268,28 @@ def frame_inputs(seed, B, H, text, frames, height, width):
     return out[0], out[1]
 
 
+def mask_layout(root: str):
+    """The reference's get_block_mask on seeded frame / inner masks (it
+    fixes B = 2, H = 30) and the query side of preprocess_qkv /
+    reverse_process_out on a token-index tensor (positions + 1, so the
+    zero padding reads 0)."""
+    import torch
+
+    sys.path.insert(0, root)
+    from special_attentions.utils import mask_related as mr
+
+    rs = np.random.RandomState(601)
+    frame = torch.from_numpy(rs.rand(2, 30, 13, 13) < 0.4)
+    inner = torch.from_numpy(rs.rand(2, 30, 22, 21) < 0.8)
+    block = mr.get_block_mask(inner, frame)
+    idx = torch.arange(1, 17777, dtype=torch.float64).view(1, 1, 17776, 1)
+    qp, _, _ = mr.preprocess_qkv(idx, idx.clone(), idx.clone())
+    back = mr.reverse_process_out(qp)
+    return {"block_mask": np.packbits(block.numpy() != 0), "block_shape": np.array(block.shape),
+            "q_processed": qp.reshape(-1).numpy().astype(np.int32),
+            "q_back": back.reshape(-1).numpy().astype(np.int32)}
+
+
 def frame_scope(root: str):
     import torch
 
@@ -390,6 +415,7 @@ def main(root: str):
         np.savez_compressed(HERE / f"{name}.npz", **out)
     np.savez_compressed(HERE / "attention_kat.npz", **attention_kat(root, bsk))
     np.savez_compressed(HERE / "frame_scope.npz", **frame_scope(root))
+    np.savez_compressed(HERE / "mask_layout.npz", **mask_layout(root))
     np.savez_compressed(HERE / "smart_layout.npz", **smart_layout(root))
     np.savez_compressed(HERE / "sta_layout.npz", **sta_layout(root))
     print("fixtures written to", HERE)

@@ -115,3 +115,30 @@ def test_forward_backup_cogvideox_shape(cuda_device):
     ref = ofs.frame_attention_rows(q, k, v, fmask, geo.text_len, geo.frame_len, 0.125, range(2), rows)
     got = out.float().cpu().numpy().reshape(2, geo.seq_len, 64)[:, rows]
     assert np.abs(got - ref).max() <= 2e-2
+
+
+def test_mask_related_mirror_on_gpu(cuda_device):
+    """special_attentions.utils.mask_related: the frame-scope mask through
+    the mirror's reference-named function (golden case, injected sample), and
+    calc_attn_block_sum_efficient = the block-size-weighted softmax numerator
+    of the mean-pooled logits, rows normalised to 1 (fp64, 1e-12)."""
+    from sparseattnfunctions_b200.special_attentions.utils import mask_related as mr
+
+    d = np.load(GOLDEN / "frame_scope.npz")
+    name, seed, B, H, text, frames, height, width, n, thr = mg.FRAME_CASES[0]
+    q64, k64 = mg.frame_inputs(seed, B, H, text, frames, height, width)
+    q, k = torch.from_numpy(q64).float().to(cuda_device), torch.from_numpy(k64).float().to(cuda_device)
+    spatial = torch.from_numpy(d[f"{name}_spatial"].astype(np.int64))
+    m = mr.generate_attention_mask_frame_scope(q, k, text_length=text, f=frames, width=width, height=height,
+                                               sample_num=n, base_threshold=thr, spatial=spatial)
+    assert np.array_equal(m.cpu().numpy(), d[f"{name}_mask"])
+
+    g = torch.Generator().manual_seed(9)
+    qq = torch.randn(1, 2, 1000, 64, generator=g).to(torch.bfloat16)
+    kk = torch.randn(1, 2, 1000, 64, generator=g).to(torch.bfloat16)
+    est = mr.calc_attn_block_sum_efficient(qq.to(cuda_device), kk.to(cuda_device), block_size=64).cpu().numpy()
+    s = osel.pooled_scores(osel.block_means(qq, 64), osel.block_means(kk, 64)) / 8.0
+    cols = np.full(16, 64.0)
+    cols[-1] = 1000 - 15 * 64
+    mass = cols * np.exp(s - s.max(-1, keepdims=True))
+    np.testing.assert_allclose(est, mass / mass.sum(-1, keepdims=True), rtol=1e-12, atol=1e-15)

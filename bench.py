@@ -464,7 +464,8 @@ def run_saf(args, world, rank, local):
     subs = [("pool", args.no_pool, lambda: bench_pool(args, dev, world, q, k, v)),
             ("merge", args.no_merge, lambda: bench_merge(args, dev, world, rank)),
             ("combined", args.no_combined, lambda: bench_combined(args, dev, world, rank)),
-            ("long", args.no_long, lambda: bench_long(args, dev, world, rank))]
+            ("long", args.no_long, lambda: bench_long(args, dev, world, rank)),
+            ("local_global", args.no_local_global, lambda: bench_local_global(args, dev, world, q, k, v))]
     for name, skip, fn in subs:
         if skip:
             continue
@@ -626,6 +627,69 @@ def bench_pool(args, dev, world, q, k, v):
             "dense_tflops": round(flop / (ms_dense * 1e-3) / 1e12, 1),
             "torch_sdpa_dense_ms": round(ms_sdpa, 4),
             "torch_sdpa_dense_tflops": round(flop / (ms_sdpa * 1e-3) / 1e12, 1), "steps": n}
+
+
+def bench_local_global(args, dev, world, q, k, v):
+    """LocalGlobalAttention (LocalGlobalAttention.py:183-259) on the config-2
+    layer: dense text + frame-0 rows, 18 patches x 2 batches over their
+    window + probe keys (7073 per list), the probe of 1280 sampled rows
+    every update_gap calls."""
+    import torch
+
+    from sparseattnfunctions_b200 import kernels
+    from sparseattnfunctions_b200.special_attentions import LocalGlobalAttention as lga
+
+    B, H, S, D = q.shape
+    stream = torch.cuda.current_stream(dev)
+    obj = lga.LocalGlobalAttention()
+    lga.counter = 0
+    obj(q, k, v)  # builds the window lists and the first probe
+    n = 5
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return allreduce(e0.elapsed_time(e1) / n, "max", world)
+
+    def forward_no_probe():
+        lga.counter = 1 << 30  # keep the current probe keys
+        obj(q, k, v)
+
+    ms_fwd = timed(forward_no_probe)
+    qv = obj.slice_video(q)
+    ms_probe = timed(lambda: obj.probe._probe(qv, k))
+    dense = lga.TEXT_LEN + 1350
+    out = torch.empty_like(q)
+    ms_dense = timed(lambda: obj.attention_text(q[:, :, :dense], k, v, out=out[:, :, :dense]))
+    kidx = obj.key_lists(qv, k)
+    lga.counter = 1 << 30
+    ms_gather_kv = timed(lambda: (kernels.gather_rows(k, kidx), kernels.gather_rows(v, kidx)))
+    qp = obj.transform_q(q)
+    kp, vp = kernels.gather_rows(k, kidx), kernels.gather_rows(v, kidx)
+    ms_patch = timed(lambda: obj.attention_video(qp, kp, vp))
+    L = kidx.shape[1]
+    flop_dense = 4.0 * B * H * dense * S * D
+    flop_patch = 4.0 * kidx.shape[0] * H * qp.shape[2] * L * D
+    flop_probe = 2 * 2.0 * B * H * 1280 * S * D
+    gather_bytes = 2 * 2 * kidx.numel() * H * D * 2  # k and v rows read and written
+    return {"workload": "LocalGlobalAttention on the config-2 layer (B=2, H=30, S=17776, D=64, bf16): dense "
+                        f"{dense} rows, 36 patch lists of {L} keys, probe of 1280 rows every 5 calls",
+            "ms_forward": round(ms_fwd, 4), "ms_probe": round(ms_probe, 4),
+            "ms_per_call_with_probe_every_5": round(ms_fwd + ms_probe / 5, 4),
+            "ms_dense_rows": round(ms_dense, 4), "ms_gather_kv": round(ms_gather_kv, 4),
+            "ms_patch_attention": round(ms_patch, 4),
+            "dense_rows_tflops": round(flop_dense / (ms_dense * 1e-3) / 1e12, 1),
+            "patch_attention_tflops": round(flop_patch / (ms_patch * 1e-3) / 1e12, 1),
+            "probe_qk_tflops": round(flop_probe / (ms_probe * 1e-3) / 1e12, 1),
+            "gather_kv_gbs": round(gather_bytes / (ms_gather_kv * 1e-3) / 1e9, 1), "steps": n}
 
 
 def bench_merge(args, dev, world, rank):
@@ -920,6 +984,7 @@ def main():
     ap.add_argument("--combined-steps", type=int, default=2)
     ap.add_argument("--no-long", action="store_true", help="skip the config-5 sequence-sharded sub-benchmark")
     ap.add_argument("--long-steps", type=int, default=10)
+    ap.add_argument("--no-local-global", action="store_true", help="skip the LocalGlobalAttention sub-benchmark")
     ap.add_argument("--no-reference-kernel", action="store_true",
                     help="skip timing the reference's own Triton kernels (baseline/_ref) at N=1")
     args = ap.parse_args()

@@ -381,6 +381,41 @@ int32_t saf_ulysses_unpack(const void* buf, int32_t T, int32_t dtype, int64_t B,
                            int64_t D, int64_t stride_b, int64_t stride_s, int64_t stride_h,
                            const int32_t* head_off, int32_t P, void* const* seq, void* stream);
 
+/* ---- (6) local + global keys (LocalGlobalAttention) -------------------
+ * Row gather: out[ob, h, s, :] = x[src / Sx, h, src % Sx, :] with
+ * src = idx[ob * So + s] (int64, flattened (batch, row) of x); src < 0
+ * writes a zero row, src >= Bx * Sx a zero row and SAF_DEV_BADINDEX.  D x
+ * element size a multiple of 16 bytes, pointers 16-byte aligned, strides in
+ * elements (multiples of 16 bytes).  Duplicated sources are allowed.
+ * Replaces: transform_q / transform_kv_v1 / transform_output
+ * (special_attentions/LocalGlobalAttention.py:212-245): the rearranges and
+ * the torch.gather of k / v by each (patch, batch) key list. */
+int32_t saf_gather_rows(const void* x, int32_t dtype, int64_t Bx, int64_t H, int64_t Sx, int64_t D,
+                        int64_t x_sb, int64_t x_sh, int64_t x_ss, void* out, int64_t Bo, int64_t So,
+                        int64_t o_sb, int64_t o_sh, int64_t o_ss, const int64_t* idx, void* stream);
+
+/* Probe mass of sampled query rows: qs [B, H, R, 64] holds the R sampled
+ * rows of every head (gathered), k [B, H, Sk, 64], both bf16 or both f16.
+ * mass_out [B, Sk] fp64 = round16(sum over heads and rows of
+ * round16(softmax_keys(round16(qs . k) / 8))), round16 = rounding to the
+ * input type, sums in fp32 in a fixed order (the reference's 16-bit matmul,
+ * softmax and sum).  tcgen05 kernel; workspace of
+ * saf_probe_workspace_bytes(B, H, Sk, R) bytes.
+ * Replaces: probe_solver._probe_num up to the masked_fill
+ * (special_attentions/LocalGlobalAttention.py:50-57). */
+size_t saf_probe_workspace_bytes(int64_t B, int64_t H, int64_t Sk, int32_t n_samp);
+int32_t saf_probe_mass(const saf_tensor4* qs, const saf_tensor4* k, void* workspace,
+                       size_t workspace_bytes, double* mass_out, void* stream);
+
+/* Masked top-n: for row r = p * B + b of out [P * B, n] int32, the n keys of
+ * largest mass[b, :] among those with local_mask[p, key] == 0 (uint8
+ * [P, Sk]), ties to the lower key, in ascending key order.  n <= the
+ * unmasked keys of every row.
+ * Replaces: the masked_fill, descending sort and slice of
+ * probe_solver._probe_num (special_attentions/LocalGlobalAttention.py:58-62). */
+int32_t saf_masked_topn(const double* mass, const uint8_t* local_mask, int64_t B, int64_t P, int64_t Sk,
+                        int32_t n, int32_t* out, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -29,7 +29,8 @@ def install_alias() -> None:
     sys.modules.setdefault("special_attentions", pkg)
     for sub in ("utils", "utils.block_sparse_attn_kernel", "utils.merge_unmerge",
                 "utils.mask_related", "utils.attn_pooling_kernel", "block_mask_attn", "MergeAttention",
-                "combined_attn", "SmartAttention", "SparseGen_Plus", "SildingTileAttention"):
+                "combined_attn", "SmartAttention", "SparseGen_Plus", "SildingTileAttention",
+                "LocalGlobalAttention"):
         try:
             mod = importlib.import_module(f"{pkg.__name__}.{sub}")
         except ImportError:

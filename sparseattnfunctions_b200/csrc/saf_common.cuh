@@ -32,6 +32,8 @@ uint64_t wait_budget_ns();
 CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank,
                            void* gaddr, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
                            const cuuint32_t* box, CUtensorMapSwizzle swizzle);
+// 4-D tensor map over a [B,H,S,D] 16-bit tensor, box `rows` x 64, 128B swizzle.
+int32_t make_qkv_map(CUtensorMap* map, const saf_tensor4* t, int rows);
 // Current device is sm_100 (B200 family).
 bool current_device_is_sm100();
 // Makes the device that owns a pointer current for one entry point and puts

@@ -62,6 +62,28 @@ CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// Builds a 4-D tensor map over a [B,H,S,D] 16-bit tensor with a box of
+// `rows` x 64 elements and 128-byte swizzle.
+int32_t make_qkv_map(CUtensorMap* map, const saf_tensor4* t, int rows) {
+  const uint64_t eb = 2;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t->D), static_cast<cuuint64_t>(t->S),
+                        static_cast<cuuint64_t>(t->H), static_cast<cuuint64_t>(t->B)};
+  uint64_t sh = static_cast<uint64_t>(t->stride_h), sb = static_cast<uint64_t>(t->stride_b);
+  // Extent-1 dims take any legal stride.
+  if (t->H == 1) sh = static_cast<uint64_t>(t->stride_s) * t->S;
+  if (t->B == 1) sb = sh * t->H;
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t->stride_s) * eb, sh * eb, sb * eb};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16 != 0 || strides[i] == 0 || strides[i] >= (1ull << 40))
+      return SAF_ERR_STRIDE;
+  cuuint32_t box[4] = {64u, static_cast<cuuint32_t>(rows), 1u, 1u};
+  const CUtensorMapDataType dt =
+      t->dtype == SAF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode_tensor_map(map, dt, 4, t->data, dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  return r == CUDA_SUCCESS ? SAF_OK : SAF_ERR_STRIDE;
+}
+
 bool current_device_is_sm100() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;

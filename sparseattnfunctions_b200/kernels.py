@@ -643,3 +643,70 @@ def ulysses_unpack(buf: torch.Tensor, outs, head_off) -> None:
         rc = _lib.load().saf_ulysses_unpack(buf.data_ptr(), T, _DTYPES[x.dtype], B, s, H, D, x.stride(0),
                                             x.stride(1), x.stride(2), offs, P, ptrs, _stream_ptr(dev))
     _lib.check("saf_ulysses_unpack", rc)
+
+
+def gather_rows(x: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Row gather across batches: ``out[ob, h, s] = x[idx[ob, s] // Sx, h,
+    idx[ob, s] % Sx]`` for ``x`` ``[Bx, H, Sx, D]`` and int64 ``idx``
+    ``[Bo, So]`` (negative entries give zero rows); ``out`` ``[Bo, H, So, D]``
+    may be a strided view (saf_gather_rows)."""
+    dev = _require_cuda(x, idx)
+    x = _d_last(x)
+    if x.dim() != 4 or idx.dim() != 2 or idx.dtype != torch.int64:
+        raise ValueError("expected x [B, H, S, D] and an int64 [Bo, So] index")
+    idx = idx.contiguous()
+    Bx, H, Sx, D = x.shape
+    Bo, So = idx.shape
+    if out is None:
+        out = torch.empty(Bo, H, So, D, dtype=x.dtype, device=dev)
+    elif tuple(out.shape) != (Bo, H, So, D) or out.dtype != x.dtype or out.stride(-1) != 1:
+        raise ValueError(f"out must be a {x.dtype} [{Bo}, {H}, {So}, {D}] tensor with contiguous rows")
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_gather_rows(x.data_ptr(), _DTYPES[x.dtype], Bx, H, Sx, D, x.stride(0), x.stride(1),
+                                         x.stride(2), out.data_ptr(), Bo, So, out.stride(0), out.stride(1),
+                                         out.stride(2), idx.data_ptr(), _stream_ptr(dev))
+    _lib.check("saf_gather_rows", rc)
+    return out
+
+
+def probe_mass(qs: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    """Probe mass ``[B, Sk]`` fp64 of the sampled rows ``qs`` ``[B, H, R, 64]``
+    over the keys ``k`` ``[B, H, Sk, 64]`` (both bf16 or both f16): the
+    16-bit softmax probabilities of every sampled row summed over rows and
+    heads, rounded as the reference's 16-bit matmul / softmax / sum
+    (saf_probe_mass, tcgen05)."""
+    dev = _require_cuda(qs, k)
+    qs, k = _d_last(qs), _d_last(k)
+    B, H, R, D = qs.shape
+    Sk = k.shape[2]
+    lib = _lib.load()
+    ws_bytes = lib.saf_probe_workspace_bytes(B, H, Sk, R)
+    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
+    mass = torch.empty(B, Sk, dtype=torch.float64, device=dev)
+    tq, tk = _t4(qs), _t4(k)
+    with torch.cuda.device(dev):
+        rc = lib.saf_probe_mass(ctypes.byref(tq), ctypes.byref(tk), ws.data_ptr(), ws.numel(), mass.data_ptr(),
+                                _stream_ptr(dev))
+    _lib.check("saf_probe_mass", rc)
+    return mass
+
+
+def masked_topn(mass: torch.Tensor, local_mask: torch.Tensor, n: int) -> torch.Tensor:
+    """int32 ``[P * B, n]``: row ``p * B + b`` lists, ascending, the n keys of
+    largest ``mass[b]`` outside ``local_mask[p]`` (ties to the lower key)
+    (saf_masked_topn)."""
+    dev = _require_cuda(mass, local_mask)
+    if mass.dtype != torch.float64 or mass.dim() != 2:
+        raise ValueError("mass must be a float64 [B, Sk] tensor")
+    if local_mask.dim() != 2 or local_mask.shape[1] != mass.shape[1]:
+        raise ValueError("local_mask must be [P, Sk]")
+    mass = mass.contiguous()
+    lm = local_mask.to(torch.uint8).contiguous()
+    B, Sk = mass.shape
+    P = lm.shape[0]
+    out = torch.empty(P * B, n, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_masked_topn(mass.data_ptr(), lm.data_ptr(), B, P, Sk, int(n), out.data_ptr(),
+                                         _stream_ptr(dev))
+    _lib.check("saf_masked_topn", rc)
+    return out

@@ -41,6 +41,13 @@ Fixtures
   mask_layout.npz   get_block_mask (utils/mask_related.py:397-404) on seeded
                     masks, and the query side of preprocess_qkv /
                     reverse_process_out (:87-187) on a token-index tensor
+  local_global.npz  LocalGlobalAttention's get_mask (LocalGlobalAttention.py:
+                    114-179: the patch window mask, remain_num and the keys
+                    its CPU sort put after the window keys) and
+                    probe_solver._probe_num (:50-62) on seeded bf16 q / k
+                    with 2 heads: the rows torch.randint drew, the summed
+                    probabilities (the softmax output summed as :57 does)
+                    and the indices it returned
 """
 from __future__ import annotations
 
@@ -311,6 +318,76 @@ def frame_scope(root: str):
     return out
 
 
+LG_PROBE = dict(seed=701, H=2, n_video=16200, S=17776, D=64)
+
+
+def lg_probe_inputs(seed, H, n_video, S, D):
+    """bf16-representable q_video [2, H, n_video, D] and k [2, H, S, D]: a
+    smooth field over the key index plus noise, so the probe mass varies."""
+    rs = np.random.RandomState(seed)
+    import torch
+
+    base = rs.randn(2, H, S // 64 + 1, D).repeat(64, axis=2)[:, :, :S]
+    k = torch.from_numpy(base + 0.7 * rs.randn(2, H, S, D)).to(torch.bfloat16)
+    q = torch.from_numpy(rs.randn(2, H, n_video, D) * 1.5).to(torch.bfloat16)
+    return q, k
+
+
+def local_global(root: str):
+    """get_mask and probe_solver._probe_num from the reference's source text
+    (the module builds its mask on CUDA when imported), run on the CPU: the
+    module constants, get_mask and probe_solver are executed alone, with
+    create_mask on the CPU and torch.softmax wrapped to record its output."""
+    import ast
+    import torch
+    from torch.nn.attention.flex_attention import create_mask as _create_mask
+
+    src = Path(root, "special_attentions", "LocalGlobalAttention.py").read_text()
+    tree = ast.parse(src)
+    consts = {"video_shape", "patch_shape", "batch_size", "compression", "sample_num", "padding",
+              "percentile", "update_gap"}
+    keep = [n for n in tree.body
+            if (isinstance(n, ast.Assign) and any(isinstance(t, ast.Name) and t.id in consts for t in n.targets))
+            or (isinstance(n, (ast.FunctionDef, ast.ClassDef)) and n.name in ("get_mask", "probe_solver"))]
+    seen = []
+
+    class _Torch(_CpuTorch):
+        def __getattr__(self, name):
+            if name == "softmax":
+                def softmax(x, *a, **k):
+                    y = torch.softmax(x, *a, **k)
+                    seen.append(y)
+                    return y
+                return softmax
+            return super().__getattr__(name)
+
+    def create_mask(fn, B, H, Q_LEN, KV_LEN, device="cuda"):
+        return _create_mask(fn, B, H, Q_LEN, KV_LEN, device="cpu")
+
+    ns = {"torch": _Torch(), "create_mask": create_mask, "print": lambda *a, **k: None}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), "local_global", "exec"), ns)
+    mask, indices = ns["get_mask"]()
+    remain = indices.shape[1]
+    out = {"mask": np.packbits(mask.numpy()), "mask_shape": np.array(mask.shape), "remain": np.array(remain)}
+    fill = [np.setdiff1d(indices[r].numpy(), np.nonzero(mask[r].numpy())[0]) for r in range(mask.shape[0])]
+    out["fill_keys"] = np.concatenate(fill).astype(np.int32)
+    out["fill_off"] = np.cumsum([0] + [f.size for f in fill]).astype(np.int32)
+    cfg = LG_PROBE
+    q, k = lg_probe_inputs(cfg["seed"], cfg["H"], cfg["n_video"], cfg["S"], cfg["D"])
+    solver = ns["probe_solver"](percentile=ns["percentile"], sample_num=ns["sample_num"], device="cpu",
+                                type="num", mask=mask)
+    torch.manual_seed(cfg["seed"])
+    samples = torch.randint(0, cfg["n_video"], (2, 1, ns["sample_num"]), device="cpu")
+    torch.manual_seed(cfg["seed"])
+    seen.clear()
+    idx = solver._probe(q, k)
+    out["samples"] = samples.reshape(2, -1).numpy().astype(np.int32)
+    # the statement after the softmax (:57), before the repeat and masked_fill
+    out["att_probs"] = seen[0].sum(dim=[1, 2]).float().numpy()
+    out["probe_indices"] = idx.numpy().astype(np.int32)
+    return out
+
+
 def closure_vars(fn):
     return {name: cell.cell_contents for name, cell in zip(fn.__code__.co_freevars, fn.__closure__)}
 
@@ -418,6 +495,7 @@ def main(root: str):
     np.savez_compressed(HERE / "mask_layout.npz", **mask_layout(root))
     np.savez_compressed(HERE / "smart_layout.npz", **smart_layout(root))
     np.savez_compressed(HERE / "sta_layout.npz", **sta_layout(root))
+    np.savez_compressed(HERE / "local_global.npz", **local_global(root))
     print("fixtures written to", HERE)
 
 

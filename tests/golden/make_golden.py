@@ -17,7 +17,10 @@ Fixtures
   energy_masks.npz  transfer_attn_to_mask(mode="energy") (SparseGen_Plus.py:12-84)
   topk_adaptive_masks.npz  transfer_attn_to_mask(mode="topk") (SparseGen_Plus.py:28-50)
   tome_*.npz        bipartite_soft_matching_video + merge / unmerge
-                    (utils/merge_unmerge.py:34-154), fp64 metric
+                    (utils/merge_unmerge.py:34-154), fp64 metric;
+                    tome_bf16_r4000.npz: the matching on a bf16 metric (the
+                    reference normalises and multiplies in bf16), its split
+                    order and the merged src / dst it chose
   sta_layout.npz    SildingTileAttention's tile-window mask_mod (small and
                     CogVideoX-2B configs) and its preprocess token order
                     (SildingTileAttention.py:18-136)
@@ -396,6 +399,7 @@ TOPK_CASES = [  # (seed, B, H, n, topk)
     (101, 1, 2, 16, 4), (102, 2, 3, 33, 5), (103, 1, 1, 139, 14), (104, 1, 2, 64, 1)]
 ENERGY_CASES = [  # (seed, B, H, n, thr, min_ratio, max_ratio)
     (201, 1, 2, 20, 0.9, 0.1, 0.8), (202, 2, 2, 45, 0.95, 0.1, 0.7), (203, 1, 3, 139, 0.98, 0.12, 1.0)]
+TOME_BF16_CASE = ("tome_bf16_r4000", 13, 16, 4000)  # (name, metric seed, C, r), no_rand split
 TOME_CASES = [  # (name, metric seed, C, r, generator seed or None)
     ("tome_norand_r4000", 11, 8, 4000, None), ("tome_gen_r9000", 12, 8, 9000, 5)]
 GEOM = dict(w=45, h=30, t=13, sx=3, sy=3, st=4)
@@ -490,6 +494,16 @@ def main(root: str):
         out["unmerge_rowsum"] = un.sum(-1).reshape(-1).numpy()
         out["unmerge_proj"] = (un @ proj).reshape(-1).numpy()
         np.savez_compressed(HERE / f"{name}.npz", **out)
+    name, seed, C, r = TOME_BF16_CASE
+    metric = torch.from_numpy(tome_metric(seed, C)).to(torch.bfloat16)
+    merge, _ = mu.bipartite_soft_matching_video(metric, **GEOM, r=r, no_rand=True)
+    cv = closure_vars(merge)
+    sv = closure_vars(cv["split"])
+    np.savez_compressed(HERE / f"{name}.npz", params=np.array([seed, C, r]),
+                        a_idx=sv["a_idx"].reshape(-1).numpy().astype(np.int16),
+                        b_idx=sv["b_idx"].reshape(-1).numpy().astype(np.int16),
+                        src_idx=cv["src_idx"].reshape(-1).numpy().astype(np.int16),
+                        dst_idx=cv["dst_idx"].reshape(-1).numpy().astype(np.int16))
     np.savez_compressed(HERE / "attention_kat.npz", **attention_kat(root, bsk))
     np.savez_compressed(HERE / "frame_scope.npz", **frame_scope(root))
     np.savez_compressed(HERE / "mask_layout.npz", **mask_layout(root))

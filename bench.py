@@ -14,7 +14,9 @@ are split over the ranks (15/15, 8/8/7/7, 4,4,4,4,4,4,3,3), B = 2 on each,
 with no collective on the data path (strong scaling; ``value`` = the
 layer's live FLOP / the slowest rank's time).  A weak-scaling number (a
 whole layer per rank) is reported beside it.  Times are CUDA-event times on
-the launching stream, max over ranks.  At one GPU q/k/v/o are 136 MB each
+the launching stream, max over ranks; the timed steps replay the selection
+and the attention as two CUDA graphs captured from the same calls, so host
+load on a shared machine cannot leave the GPU idle inside the timed region.  At one GPU q/k/v/o are 136 MB each
 (larger than the 126 MB L2), so no L2 flush is needed between steps.
 
 At N = 1 the reference's own Triton kernels (installed unmodified in
@@ -282,9 +284,41 @@ def run_saf(args, world, rank, local):
             ev[2].record(stream)
         return step
 
+    def make_graph_step(qq, kk, vv, oo, holder):
+        """The same two launches sequences captured as CUDA graphs (selection,
+        attention), replayed on the stream: the host enqueues a step in a few
+        microseconds, so a busy or descheduled host never leaves the GPU idle
+        inside the timed region."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                holder[0] = kernels.pool_topk(qq, kk, **sel_kw)
+                kernels.bsa_fwd(qq, kk, vv, holder[0], scale, out=oo)
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        g_sel, g_att = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_sel):
+            holder[0] = kernels.pool_topk(qq, kk, **sel_kw)
+        with torch.cuda.graph(g_att):
+            kernels.bsa_fwd(qq, kk, vv, holder[0], scale, out=oo)
+        torch.cuda.synchronize()
+        holder.append((g_sel, g_att))  # keep the graphs alive
+
+        def step(ev):
+            ev[0].record(stream)
+            g_sel.replay()
+            ev[1].record(stream)
+            g_att.replay()
+            ev[2].record(stream)
+        return step
+
     held = [None]
-    step = make_step(q, k, v, out, held)
     dummy = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))]
+    for _ in range(args.warmup):
+        make_step(q, k, v, out, held)(dummy[0])
+    torch.cuda.synchronize()
+    step = make_graph_step(q, k, v, out, held)
     for _ in range(args.warmup):
         step(dummy[0])
     torch.cuda.synchronize()
@@ -312,7 +346,7 @@ def run_saf(args, world, rank, local):
         qf, kf, vf = q_full.to(dev), k_full.to(dev), v_full.to(dev)
         of = torch.empty_like(qf)
         wheld = [None]
-        wstep = make_step(qf, kf, vf, of, wheld)
+        wstep = make_graph_step(qf, kf, vf, of, wheld)
         for _ in range(3):
             wstep(dummy[0])
         torch.cuda.synchronize()

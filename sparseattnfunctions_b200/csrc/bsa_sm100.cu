@@ -101,77 +101,88 @@ struct BsaParams {
   // [next tile, CTAs done] counters (zero on entry; the last CTA resets them)
   int n_tiles, BH;
   unsigned int* tile_ctr;
+  int list_cap;  // entries of a tile's block list in shared memory (nbk rounded up to 8)
 };
 
-// Iterates the live kv tiles of one 128-row query tile.  With 64-row mask
-// blocks the tile covers two mask rows; their (ascending) column lists are
-// merged and every tile carries a 2-bit row mask: bit 0 = rows [0,64) live,
-// bit 1 = rows [64,128) live.  Every role of the CTA runs its own copy, so
-// all of them see the same sequence.  Out-of-range columns are skipped.
-struct TileIter {
-  const int32_t* cols;
-  int32_t p0, e0, p1, e1;  // CSR offsets are int32 by contract
-  int nbk;
-  bool two_rows;
-  unsigned int* status;
-
-  __device__ void init(const BsaParams& p, int g, int tile) {
-    cols = p.col_idx;
-    nbk = p.nbk;
-    status = p.status;
-    const int32_t* rp = p.row_ptr + static_cast<int64_t>(g) * (p.nbq + 1);
-    auto clampi = [&](int32_t x) -> int32_t {
-      return x < 0 ? 0 : (static_cast<int64_t>(x) > p.col_capacity ? static_cast<int32_t>(p.col_capacity) : x);
-    };
-    two_rows = (p.bm == 64);
-    const int r0 = two_rows ? 2 * tile : tile;
-    p0 = clampi(rp[r0]);
-    e0 = clampi(rp[r0 + 1]);
-    p1 = e1 = 0;
-    if (two_rows && r0 + 1 < p.nbq) {
-      p1 = clampi(rp[r0 + 1]);
-      e1 = clampi(rp[r0 + 2]);
-    }
-  }
-  __device__ bool valid(int c) {
-    if (c >= 0 && c < nbk) return true;
-    atomicOr(status, SAF_DEV_BADINDEX);
-    return false;
-  }
-  __device__ bool next(int& col, uint32_t& rmask) {
-    while (true) {
-      const bool h0 = p0 < e0, h1 = p1 < e1;
-      if (!h0 && !h1) return false;
-      int c;
-      uint32_t m;
-      if (!two_rows) {
-        c = cols[p0++];
-        m = 3u;
-      } else {
-        const int c0 = h0 ? cols[p0] : 0x7fffffff;
-        const int c1 = h1 ? cols[p1] : 0x7fffffff;
-        if (c0 <= c1) {
-          c = c0;
-          m = 1u;
-          ++p0;
-          if (c1 == c0) {
-            m |= 2u;
-            ++p1;
-          }
-        } else {
-          c = c1;
-          m = 2u;
-          ++p1;
-        }
+// Builds the live key blocks of one 128-row query tile into a list in shared
+// memory (uint16 entries: column | row mask << 14) and returns its length;
+// the 32 lanes of the producer warp build it together, before the tile is
+// handed to the other roles, which then read it from shared memory.  With
+// 64-row mask blocks the tile covers two mask rows: their column lists are
+// merged through two bitmaps of the key blocks (ascending, a column listed by
+// both rows once) and the row mask says which half is live (bit 0 = rows
+// [0,64), bit 1 = rows [64,128)).  Out-of-range columns are skipped and set
+// the bad-index flag.
+__device__ int build_tile_list(const BsaParams& p, int g, int tile, uint16_t* lst, uint32_t* bits, int lane) {
+  const int32_t* rp = p.row_ptr + static_cast<int64_t>(g) * (p.nbq + 1);
+  auto clampi = [&](int32_t x) -> int32_t {
+    return x < 0 ? 0 : (static_cast<int64_t>(x) > p.col_capacity ? static_cast<int32_t>(p.col_capacity) : x);
+  };
+  const bool two_rows = (p.bm == 64);
+  const int r0 = two_rows ? 2 * tile : tile;
+  const int p0 = clampi(rp[r0]), e0 = clampi(rp[r0 + 1]);
+  const uint32_t below = (1u << lane) - 1u;
+  int n = 0;
+  if (!two_rows) {
+    for (int base = p0; base < e0; base += 32) {
+      const int i = base + lane;
+      int c = -1;
+      bool v = false;
+      if (i < e0) {
+        c = p.col_idx[i];
+        v = c >= 0 && c < p.nbk;
+        if (!v) atomicOr(p.status, SAF_DEV_BADINDEX);
       }
-      if (valid(c)) {
-        col = c;
-        rmask = m;
-        return true;
-      }
+      const uint32_t m = __ballot_sync(0xffffffffu, v);
+      if (v) lst[n + __popc(m & below)] = static_cast<uint16_t>(c | (3 << 14));
+      n += __popc(m);
     }
+    return n;
   }
-};
+  int p1 = 0, e1 = 0;
+  if (r0 + 1 < p.nbq) {
+    p1 = clampi(rp[r0 + 1]);
+    e1 = clampi(rp[r0 + 2]);
+  }
+  const int words = (p.nbk + 31) >> 5;
+  uint32_t* ba = bits;
+  uint32_t* bb = bits + words;
+  for (int w = lane; w < 2 * words; w += 32) bits[w] = 0u;
+  __syncwarp();
+  auto mark = [&](int s, int e, uint32_t* set) {
+    for (int i = s + lane; i < e; i += 32) {
+      const int c = p.col_idx[i];
+      if (c >= 0 && c < p.nbk)
+        atomicOr(set + (c >> 5), 1u << (c & 31));
+      else
+        atomicOr(p.status, SAF_DEV_BADINDEX);
+    }
+  };
+  mark(p0, e0, ba);
+  mark(p1, e1, bb);
+  __syncwarp();
+  for (int w0 = 0; w0 < words; w0 += 32) {
+    const int w = w0 + lane;
+    const uint32_t a = w < words ? ba[w] : 0u, b = w < words ? bb[w] : 0u;
+    uint32_t u = a | b;
+    const int cnt = __popc(u);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += y;
+    }
+    int pos = n + incl - cnt;
+    while (u != 0u) {
+      const int bit = __ffs(u) - 1;
+      u &= u - 1u;
+      const uint32_t rmask = ((a >> bit) & 1u) | (((b >> bit) & 1u) << 1);
+      lst[pos++] = static_cast<uint16_t>((w * 32 + bit) | (rmask << 14));
+    }
+    n += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  return n;
+}
 
 // exp2 on the FMA pipe (for part of the elements, to offload the MUFU):
 // 2^x = 2^n * 2^f with n = rint(x) (from adding 1.5 * 2^23) and
@@ -232,9 +243,13 @@ struct Layout {
   //           q_empty, tile_full[2], tile_empty[2]
   static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 10;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kBytes = kOffMisc + 16;
+  // tile lists (runtime size, after the fixed part): 2 slots of list_cap
+  // uint16 entries, then two bitmaps of the key blocks
+  static constexpr int kOffList = kOffMisc + 32;
+  static constexpr int kBytes = kOffList;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
 };
+inline int list_smem_bytes(int list_cap, int nbk) { return 2 * list_cap * 2 + 2 * ((nbk + 31) / 32) * 4; }
 
 // Masks applied inside a visited block, besides the ragged tail: none, the
 // per-row key intervals of row_ranges, or the per-head frame masks.
@@ -295,6 +310,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   volatile int* tile_slot = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);  // [2]
+  volatile int* tile_cnt = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 16);  // [2] list lengths
+  uint16_t* list_base = reinterpret_cast<uint16_t*>(smem + L::kOffList);            // [2][list_cap]
+  uint32_t* list_bits = reinterpret_cast<uint32_t*>(smem + L::kOffList + 4 * p.list_cap);
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
@@ -349,7 +367,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 0) {
     // ------------------------------------------------------------ producer
     int nk = 0, nv = 0, nq = 0, ti = 0, col;  // K / V / Q loads issued, tiles fetched
-    uint32_t rm;
     bool ok = true;
     while (ok) {
       // next tile: fetched by lane 0, published in ring slot ti & 1
@@ -359,15 +376,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int slot = ti & 1;
       ok = mbar_wait(bar_tile_empty(slot), ((ti >> 1) & 1) ^ 1, abort_flag, p.status, p.budget_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
+      int tile = 0, g = 0, n_blk = 0;
+      uint16_t* lst = list_base + slot * p.list_cap;
+      if (lin < n_total) {
+        tile_of(lin, tile, g);
+        n_blk = build_tile_list(p, g, tile, lst, list_bits, lane);
+      }
+      __threadfence_block();
+      __syncwarp();
       if (lane == 0) {
         tile_slot[slot] = lin;
+        tile_cnt[slot] = n_blk;
         mbar_arrive(bar_tile_full(slot));
       }
       __syncwarp();
       ++ti;
       if (lin >= n_total) break;
-      int tile, g;
-      tile_of(lin, tile, g);
       const int b = g / p.H, h = g % p.H;
       // Q of this tile once the previous tile's QK^T products are done
       ok = mbar_wait(bar_q_empty, (nq & 1) ^ 1, abort_flag, p.status, p.budget_ns);
@@ -377,9 +401,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_4d(sQ, &tm_q, bar_q, 0, tile * kBM, h, b);
       }
       ++nq;
-      TileIter it;
-      it.init(p, g, tile);
-      while (it.next(col, rm)) {
+      for (int jb = 0; jb < n_blk; ++jb) {
+        col = lst[jb] & 0x3fff;
         const int sk = nk % kKS, sv = nv % kVS;
         const uint32_t pk = (nk / kKS) & 1, pv = (nv / kVS) & 1;
         // this block's key biases (loads in flight across the K-stage wait)
@@ -469,27 +492,23 @@ __global__ void __launch_bounds__(kThreads, 2)
         return true;
       };
 
-      int ti = 0, nq = 0, jbase = 0, col;  // tiles taken, Q tiles used, blocks of earlier tiles
-      uint32_t rm;
+      int ti = 0, nq = 0, jbase = 0;  // tiles taken, Q tiles used, blocks of earlier tiles
       bool ok = true;
       while (ok) {
         const int slot = ti & 1;
         if (!mbar_wait(bar_tile_full(slot), (ti >> 1) & 1, abort_flag, p.status, p.budget_ns)) break;
         const int lin = tile_slot[slot];
+        const int n_blk = tile_cnt[slot];  // the MMAs need only the block count
         mbar_arrive(bar_tile_empty(slot));
         ++ti;
         if (lin >= n_total) break;
-        int tile, g;
-        tile_of(lin, tile, g);
         if (!mbar_wait(bar_q, nq & 1, abort_flag, p.status, p.budget_ns)) break;
         ++nq;
         tc_fence_after();
-        TileIter it;
-        it.init(p, g, tile);
         int j = 0;  // blocks of this tile
         bool finished = false;
         while (true) {
-          if (!it.next(col, rm)) {
+          if (j >= n_blk) {
             finished = true;
             break;
           }
@@ -569,9 +588,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       break;
     }
     const int lin = tile_slot[slot];
-    mbar_arrive(bar_tile_empty(slot));
+    const int n_blk = tile_cnt[slot];
     ++ti;
-    if (lin >= n_total) break;
+    if (lin >= n_total) {
+      mbar_arrive(bar_tile_empty(slot));
+      break;
+    }
     int tile, g;
     tile_of(lin, tile, g);
     const int b = g / p.H, h = g % p.H;
@@ -597,10 +619,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         fbits = __ldg(p.frame_bits + static_cast<int64_t>(g) * p.frames + fq);
       }
     }
-    TileIter it;
-    it.init(p, g, tile);
+    const uint16_t* lst = list_base + slot * p.list_cap;
     int j = 0;  // blocks of this tile
-    while (it.next(col, rm)) {
+    while (j < n_blk) {
+      const uint32_t ent = lst[j];
+      col = static_cast<int>(ent & 0x3fffu);
+      rm = ent >> 14;
       const int jg = jbase + j;
       if (!__all_sync(0xffffffffu,
                       mbar_wait(bar_s_full, jg & 1, abort_flag, p.status, p.budget_ns))) {
@@ -776,6 +800,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(bar_p_full);
       ++j;
     }
+    // the tile's block list is no longer read: the producer may refill the slot
+    mbar_arrive(bar_tile_empty(slot));
 
     // ---------------------------------------------------------- epilogue
     // O is read back 32 columns at a time, normalised by 1/l and stored.  A
@@ -861,7 +887,8 @@ template <int BN, bool kBias, bool kBF16, int kMask>
 int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                        BsaParams p, int n_tiles, cudaStream_t stream) {
   auto kern = bsa_fwd_sm100_kernel<BN, kBias, kBF16, kMask>;
-  const int smem = Layout<BN, kBias>::kDynSmem;
+  p.list_cap = (p.nbk + 7) / 8 * 8;
+  const int smem = Layout<BN, kBias>::kDynSmem + list_smem_bytes(p.list_cap, p.nbk);
   SAF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   // setmaxnreg.inc only draws on the registers the CTA was launched with: a
   // build that launched with fewer than the split needs would wait forever
@@ -911,6 +938,7 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   p.bm = bm;
   p.nbq = static_cast<int>((q->S + bm - 1) / bm);
   p.nbk = static_cast<int>((k->S + bn - 1) / bn);
+  if (p.nbk > 16384) return SAF_ERR_UNSUPPORTED;  // 14-bit columns in the tile lists
   p.col_capacity = col_capacity;
   p.row_ptr = row_ptr;
   p.col_idx = col_idx;

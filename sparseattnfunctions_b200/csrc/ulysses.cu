@@ -15,6 +15,7 @@
 //
 // One thread per 16-byte vector of a D row; D * element size must be a
 // multiple of 16 bytes and every row start 16-byte aligned (host-checked).
+#include <algorithm>
 #include <cstdint>
 
 #include "saf_common.cuh"
@@ -34,34 +35,54 @@ struct UlyssesParams {
   int32_t T, B, s, D, vec;   // vec = 16-byte vectors per D row
 };
 
-// kPack: seq -> buf; otherwise buf -> seq.  One thread per 16-byte vector
-// (consecutive lanes cover consecutive vectors of a row: coalesced on both
-// sides), 32-bit index arithmetic.
+// kPack: seq -> buf; otherwise buf -> seq.  A chunk row is one (s, b) pair
+// of T * h_j * vec 16-byte vectors, contiguous in buf.  threadIdx.x fixes a
+// thread's (t, h, vector) positions within a row for the whole launch (the
+// only divisions by T, h_j and vec), threadIdx.y and the grid-stride loop
+// pick rows; consecutive lanes cover consecutive vectors of buf and of a D
+// row, so both sides stay coalesced.
 template <bool kPack>
-__global__ void __launch_bounds__(256) ulysses_copy_kernel(const UlyssesParams p) {
+__global__ void __launch_bounds__(1024) ulysses_copy_kernel(const UlyssesParams p) {
   const int j = blockIdx.y;
   const int hj = p.head_off[j + 1] - p.head_off[j];
-  const int total = p.s * p.B * p.T * hj * p.vec;
-  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= total) return;
-  // chunk order: (s, b, t, h, vector)
-  const int v = idx % p.vec;
-  const int r = idx / p.vec;
-  const int h = r % hj;
-  const int q1 = r / hj;
-  const int t = q1 % p.T;
-  const int q2 = q1 / p.T;
-  const int b = q2 % p.B;
-  const int s = q2 / p.B;
+  const int inner = p.T * hj * p.vec;
   const int64_t elem_bytes = 16LL * p.vec / p.D;  // vec = D * element size / 16
-  uint4* bufv = reinterpret_cast<uint4*>(static_cast<char*>(p.buf) + p.chunk_off[j] * elem_bytes) + idx;
-  uint4* seqv = reinterpret_cast<uint4*>(static_cast<char*>(p.seq[t]) +
-                                         (static_cast<int64_t>(b) * p.s_b + static_cast<int64_t>(s) * p.s_s +
-                                          static_cast<int64_t>(p.head_off[j] + h) * p.s_h) * elem_bytes) + v;
-  if constexpr (kPack) {
-    *bufv = __ldg(seqv);
-  } else {
-    *seqv = __ldg(bufv);
+  const int64_t sb_v = p.s_b * elem_bytes / 16, ss_v = p.s_s * elem_bytes / 16;  // strides in vectors
+  const int rows = p.s * p.B;
+  uint4* buf0 = reinterpret_cast<uint4*>(static_cast<char*>(p.buf) + p.chunk_off[j] * elem_bytes);
+  for (int i = threadIdx.x; i < inner; i += blockDim.x) {
+    const int v = i % p.vec;
+    const int th = i / p.vec;
+    const int h = th % hj;
+    const int t = th / hj;
+    uint4* seq0 = reinterpret_cast<uint4*>(static_cast<char*>(p.seq[t]) +
+                                           static_cast<int64_t>(p.head_off[j] + h) * p.s_h * elem_bytes) + v;
+    // four rows per step: four independent loads in flight per thread
+    const int stride = gridDim.x * blockDim.y;
+    for (int row0 = blockIdx.x * blockDim.y + threadIdx.y; row0 < rows; row0 += 4 * stride) {
+      uint4 val[4];
+      uint4* dst[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = row0 + u * stride;
+        dst[u] = nullptr;
+        if (row < rows) {
+          const int s = row / p.B, b = row - s * p.B;
+          uint4* bv = buf0 + static_cast<int64_t>(row) * inner + i;
+          uint4* sv = seq0 + b * sb_v + s * ss_v;
+          if constexpr (kPack) {
+            val[u] = __ldg(sv);
+            dst[u] = bv;
+          } else {
+            val[u] = __ldg(bv);
+            dst[u] = sv;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (dst[u] != nullptr) *dst[u] = val[u];
+    }
   }
 }
 
@@ -113,15 +134,20 @@ int32_t ulysses_launch(bool pack, void* const* seq, int32_t T, int32_t dtype, in
   int32_t rc;
   DeviceScope dev_scope;
   if ((rc = dev_scope.bind(buf)) != SAF_OK) return rc;
-  const int64_t most = s * B * T * static_cast<int64_t>(hmax) * p.vec;  // vectors of the largest chunk
-  if (most == 0) return SAF_OK;
-  if (most >= (int64_t(1) << 31)) return SAF_ERR_SHAPE;
-  dim3 grid(static_cast<unsigned>((most + 255) / 256), static_cast<unsigned>(P));
+  const int64_t inner = static_cast<int64_t>(T) * hmax * p.vec;  // vectors per row of the largest chunk
+  if (inner == 0) return SAF_OK;
+  if (s * B >= (int64_t(1) << 31) || inner >= (int64_t(1) << 31)) return SAF_ERR_SHAPE;
+  // x: the vectors of one row (a warp multiple, at most 1024), y: rows per CTA
+  const unsigned bx = static_cast<unsigned>(std::min<int64_t>(1024, (inner + 31) / 32 * 32));
+  const unsigned by = std::max(1u, 256u / bx);
+  const int64_t row_blocks = (s * B + by - 1) / by;
+  dim3 block(bx, by);
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(row_blocks, 148 * 16)), static_cast<unsigned>(P));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (pack)
-    ulysses_copy_kernel<true><<<grid, 256, 0, st>>>(p);
+    ulysses_copy_kernel<true><<<grid, block, 0, st>>>(p);
   else
-    ulysses_copy_kernel<false><<<grid, 256, 0, st>>>(p);
+    ulysses_copy_kernel<false><<<grid, block, 0, st>>>(p);
   SAF_CUDA_TRY(cudaGetLastError());
   return SAF_OK;
 }

@@ -19,8 +19,10 @@ q / k / v.  Attention needs whole sequences, so ``UlyssesAttention``
 
 Every (b, h) is independent in selection and attention, so the only data
 movement is the two all-to-alls; when the input is not sequence-sharded,
-heads are simply partitioned with no collective.  The reference itself is
-single-GPU.
+heads are simply partitioned with no collective.  On one rank there is no
+exchange and no pack: the kernels read ``[B, S, H, D]`` in place as strided
+``[B, H, S, D]`` views and write the output rows in place.  The reference
+itself is single-GPU.
 
 ``pack`` / ``unpack`` / ``all_to_all`` default to the library kernels and
 ``torch.distributed``; tests inject host versions to check the exchange
@@ -78,25 +80,27 @@ class UlyssesAttention:
         off = self.head_off
         h = off[r + 1] - off[r]
         hs = [off[j + 1] - off[j] for j in range(P)]
-        send = self.pack([q, k, v], off)
         if P == 1:
-            recv = send
-        else:
-            recv = torch.empty(S * B * 3 * h * D, dtype=q.dtype, device=q.device)
-            self.all_to_all(recv, send, [n * B * 3 * h * D for n in lens], [s * B * 3 * hj * D for hj in hs],
-                            self.group)
+            # one rank holds every head and the whole sequence: the kernels
+            # read the [B, S, H, D] inputs as strided [B, H, S, D] views and
+            # write the output rows in place, no pack / unpack
+            out = torch.empty(B, s, H, D, dtype=q.dtype, device=q.device)
+            self.inner(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), out=out.transpose(1, 2))
+            self.last = {"S": S, "local_heads": H, "send_elems": 0, "recv_elems": 0}
+            return out
+        send = self.pack([q, k, v], off)
+        recv = torch.empty(S * B * 3 * h * D, dtype=q.dtype, device=q.device)
+        self.all_to_all(recv, send, [n * B * 3 * h * D for n in lens], [s * B * 3 * hj * D for hj in hs],
+                        self.group)
         grid = recv[:S * B * 3 * h * D].view(S, B, 3, h, D)
         qh, kh, vh = (grid[:, :, t].permute(1, 2, 0, 3) for t in range(3))
         o_rows = torch.empty(S, B, h, D, dtype=q.dtype, device=q.device)
         oh = o_rows.permute(1, 2, 0, 3)
         if h > 0:
             self.inner(qh, kh, vh, out=oh)
-        if P == 1:
-            back = o_rows.view(-1)
-        else:
-            back = torch.empty(s * B * H * D, dtype=q.dtype, device=q.device)
-            self.all_to_all(back, o_rows.view(-1), [s * B * hj * D for hj in hs], [n * B * h * D for n in lens],
-                            self.group)
+        back = torch.empty(s * B * H * D, dtype=q.dtype, device=q.device)
+        self.all_to_all(back, o_rows.view(-1), [s * B * hj * D for hj in hs], [n * B * h * D for n in lens],
+                        self.group)
         out = torch.empty(B, s, H, D, dtype=q.dtype, device=q.device)
         self.unpack(back, [out], off)
         self.last = {"S": S, "local_heads": h, "send_elems": send.numel(), "recv_elems": recv.numel()}

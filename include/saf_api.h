@@ -407,6 +407,23 @@ size_t saf_probe_workspace_bytes(int64_t B, int64_t H, int64_t Sk, int32_t n_sam
 int32_t saf_probe_mass(const saf_tensor4* qs, const saf_tensor4* k, void* workspace,
                        size_t workspace_bytes, double* mass_out, void* stream);
 
+/* Attention over per-batch key lists: o[b, h, i] = softmax over the keys
+ * j < key_len of (sm_scale * q[b, h, i] . k[sb, h, key_list[b, j]]) applied
+ * to v[sb, h, key_list[b, j]], sb = key_batch[b] -- every listed key once
+ * per listing (a repeated key counts twice, as the reference's gather +
+ * SDPA).  q / o [Bq, H, Sq, 64], k / v [B_src, H, S_src, 64] bf16 or f16 with
+ * contiguous rows (they are read as one array of 64-element rows by TMA
+ * gather4 loads, four key rows per load, no gathered copy in HBM);
+ * key_list [Bq, key_len] int32, key_batch [Bq] int32 (out-of-range entries
+ * read row 0 and set SAF_DEV_BADINDEX).  Tensor-core kernel (sm_100a).
+ * Replaces: transform_kv_v1 + attention_video of LocalGlobalAttention
+ * (special_attentions/LocalGlobalAttention.py:219-238, 207-210): the
+ * torch.gather of k / v by each (patch, batch) key list and the SDPA over
+ * the gathered rows. */
+int32_t saf_bsa_fwd_keys(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                         const saf_tensor4* o, const int32_t* key_list, int32_t key_len,
+                         const int32_t* key_batch, float sm_scale, void* stream);
+
 /* Masked top-n: for row r = p * B + b of out [P * B, n] int32, the n keys of
  * largest mass[b, :] among those with local_mask[p, key] == 0 (uint8
  * [P, Sk]), ties to the lower key, in ascending key order.  n <= the

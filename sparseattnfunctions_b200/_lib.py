@@ -146,6 +146,7 @@ SIGNATURES = {
     "saf_probe_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
     "saf_probe_mass": (_I32, [_PT4, _PT4, _P, _SZ, _P, _P]),
     "saf_masked_topn": (_I32, [_P, _P, _I64, _I64, _I64, _I32, _P, _P]),
+    "saf_bsa_fwd_keys": (_I32, [_PT4, _PT4, _PT4, _PT4, _P, _I32, _P, _F32, _P]),
 }
 
 _lib = None

@@ -18,6 +18,9 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
                       const FrameMaskArgs* frames, float* pool_rmax, float* pool_lse,
                       cudaStream_t stream);
+int32_t bsa_fwd_sm100_keys(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                           const saf_tensor4* o, const int32_t* key_list, int32_t key_len,
+                           const int32_t* key_batch, float sm_scale, cudaStream_t stream);
 
 namespace {
 
@@ -349,4 +352,25 @@ extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const
                                float sm_scale, int32_t lead_rows, void* stream) {
   return saf_bsa_fwd_ranges(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                             kv_bias_stride_bh, sm_scale, lead_rows, nullptr, stream);
+}
+
+extern "C" int32_t saf_bsa_fwd_keys(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                                    const saf_tensor4* o, const int32_t* key_list, int32_t key_len,
+                                    const int32_t* key_batch, float sm_scale, void* stream) {
+  int32_t rc;
+  for (const saf_tensor4* t : {q, k, v, o})
+    if ((rc = check_tensor4(t)) != SAF_OK) return rc;
+  if (key_list == nullptr || key_batch == nullptr) return SAF_ERR_ARG;
+  if (k->dtype != q->dtype || v->dtype != q->dtype || o->dtype != q->dtype) return SAF_ERR_DTYPE;
+  if (q->dtype == SAF_F32) return SAF_ERR_UNSUPPORTED;
+  if (v->B != k->B || v->H != k->H || v->S != k->S || k->H != q->H || k->D != q->D || v->D != q->D)
+    return SAF_ERR_SHAPE;
+  if (o->B != q->B || o->H != q->H || o->S != q->S || o->D != q->D) return SAF_ERR_SHAPE;
+  if (key_len <= 0 || q->S > 0x7fffffff) return SAF_ERR_SHAPE;
+  for (const saf_tensor4* t : {q, k, v, o})
+    if ((reinterpret_cast<uintptr_t>(t->data) & 15) != 0) return SAF_ERR_STRIDE;
+  if (o->stride_s % 8 != 0 || o->stride_h % 8 != 0 || o->stride_b % 8 != 0) return SAF_ERR_STRIDE;
+  DeviceScope dev_scope;
+  if ((rc = dev_scope.bind(q->data)) != SAF_OK) return rc;
+  return bsa_fwd_sm100_keys(q, k, v, o, key_list, key_len, key_batch, sm_scale, static_cast<cudaStream_t>(stream));
 }

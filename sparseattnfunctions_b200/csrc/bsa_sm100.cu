@@ -102,18 +102,30 @@ struct BsaParams {
   int n_tiles, BH;
   unsigned int* tile_ctr;
   int list_cap;  // entries of a tile's block list in shared memory (nbk rounded up to 8)
+  int dense;     // every key block live (no CSR)
+  // key-list mode: the keys of attention batch b are rows key_list[b, :key_len)
+  // of batch key_batch[b] of k / v ([B_src, H, key_src_len, D] contiguous),
+  // fetched row by row with TMA gather4 loads
+  const int32_t* key_list;
+  const int32_t* key_batch;
+  int key_len, key_src_len, key_src_batches;
 };
 
 // Builds the live key blocks of one 128-row query tile into a list in shared
 // memory (uint16 entries: column | row mask << 14) and returns its length;
 // the 32 lanes of the producer warp build it together, before the tile is
 // handed to the other roles, which then read it from shared memory.  With
+// `dense` set every key block is listed (no CSR is read).  With
 // 64-row mask blocks the tile covers two mask rows: their column lists are
 // merged through two bitmaps of the key blocks (ascending, a column listed by
 // both rows once) and the row mask says which half is live (bit 0 = rows
 // [0,64), bit 1 = rows [64,128)).  Out-of-range columns are skipped and set
 // the bad-index flag.
 __device__ int build_tile_list(const BsaParams& p, int g, int tile, uint16_t* lst, uint32_t* bits, int lane) {
+  if (p.dense) {  // every key block, no CSR
+    for (int j = lane; j < p.nbk; j += 32) lst[j] = static_cast<uint16_t>(j | (3 << 14));
+    return p.nbk;
+  }
   const int32_t* rp = p.row_ptr + static_cast<int64_t>(g) * (p.nbq + 1);
   auto clampi = [&](int32_t x) -> int32_t {
     return x < 0 ? 0 : (static_cast<int64_t>(x) > p.col_capacity ? static_cast<int32_t>(p.col_capacity) : x);
@@ -254,6 +266,20 @@ inline int list_smem_bytes(int list_cap, int nbk) { return 2 * list_cap * 2 + 2 
 // Masks applied inside a visited block, besides the ragged tail: none, the
 // per-row key intervals of row_ranges, or the per-head frame masks.
 constexpr int kMaskNone = 0, kMaskRanges = 1, kMaskFrames = 2;
+// Key-list mode (no mask besides the ragged tail; K / V rows by gather4).
+constexpr int kMaskKeys = 3;
+
+// TMA gather4: four rows (coordinates r0..r3 of a 2-D map whose box is one
+// row of 64 elements) into 4 x 128 bytes of shared memory, 128-byte swizzle
+// applied as for a tile load.  No multicast.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int r0,
+                                            int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
 
 template <int BN, bool kBias, bool kBF16, int kMask>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -261,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const BsaParams p) {
   using L = Layout<BN, kBias>;
+  static_assert(kMask != kMaskKeys || (BN == 128 && !kBias), "key lists: 128-key blocks, no bias");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -401,10 +428,45 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_4d(sQ, &tm_q, bar_q, 0, tile * kBM, h, b);
       }
       ++nq;
+      // key-list mode: this tile's list (the keys of its batch) and the row
+      // base of its source head in the flat [B_src*H*S_src] row view of k / v;
+      // each lane fetches four keys of a block, one block ahead of its loads
+      const int32_t* kl = nullptr;
+      int kbase = 0, knext[4] = {0, 0, 0, 0};
+      auto fetch_keys = [&](int blk) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int jj = blk * BN + 4 * lane + u;
+          knext[u] = jj < p.key_len ? kl[jj] : 0;  // rows past the list are masked in the softmax
+        }
+      };
+      if constexpr (kMask == kMaskKeys) {
+        int sb = p.key_batch[b];
+        if (sb < 0 || sb >= p.key_src_batches) {
+          atomicOr(p.status, SAF_DEV_BADINDEX);
+          sb = 0;
+        }
+        kbase = (sb * p.H + h) * p.key_src_len;
+        kl = p.key_list + static_cast<int64_t>(b) * p.key_len;
+        if (n_blk > 0) fetch_keys(lst[0] & 0x3fff);
+      }
       for (int jb = 0; jb < n_blk; ++jb) {
         col = lst[jb] & 0x3fff;
         const int sk = nk % kKS, sv = nv % kVS;
         const uint32_t pk = (nk / kKS) & 1, pv = (nv / kVS) & 1;
+        int kr[4] = {0, 0, 0, 0};
+        if constexpr (kMask == kMaskKeys) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            int kv = knext[u];
+            if (kv < 0 || kv >= p.key_src_len) {
+              atomicOr(p.status, SAF_DEV_BADINDEX);
+              kv = 0;
+            }
+            kr[u] = kbase + kv;
+          }
+          if (jb + 1 < n_blk) fetch_keys(lst[jb + 1] & 0x3fff);  // in flight across this block's waits
+        }
         // this block's key biases (loads in flight across the K-stage wait)
         float bvals[BN / 32];
         if constexpr (kBias) {
@@ -417,7 +479,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         ok = mbar_wait(bar_k_empty(sk), pk ^ 1, abort_flag, p.status, p.budget_ns);
         if (!__all_sync(0xffffffffu, ok)) break;
-        if (lane == 0) {
+        if constexpr (kMask == kMaskKeys) {
+          if (lane == 0) mbar_arrive_expect_tx(bar_k_full(sk), L::kKVBytes);
+          __syncwarp();
+          tma_gather4(sK0 + sk * L::kKVBytes + lane * 512, &tm_k, bar_k_full(sk), 0, kr[0], kr[1], kr[2], kr[3]);
+        } else if (lane == 0) {
           mbar_arrive_expect_tx(bar_k_full(sk), L::kKVBytes);
           tma_load_4d(sK0 + sk * L::kKVBytes, &tm_k, bar_k_full(sk), 0, col * BN, h, b);
         }
@@ -443,7 +509,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         ++nk;
         ok = mbar_wait(bar_v_empty(sv), pv ^ 1, abort_flag, p.status, p.budget_ns);
         if (!__all_sync(0xffffffffu, ok)) break;
-        if (lane == 0) {
+        if constexpr (kMask == kMaskKeys) {
+          if (lane == 0) mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
+          __syncwarp();
+          tma_gather4(sV0 + sv * L::kKVBytes + lane * 512, &tm_v, bar_v_full(sv), 0, kr[0], kr[1], kr[2], kr[3]);
+        } else if (lane == 0) {
           mbar_arrive_expect_tx(bar_v_full(sv), L::kKVBytes);
           tma_load_4d(sV0 + sv * L::kKVBytes, &tm_v, bar_v_full(sv), 0, col * BN, h, b);
         }
@@ -988,6 +1058,63 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   SAF_BSA_CASE(64, false, false, kMaskFrames)
 #undef SAF_BSA_CASE
   return SAF_ERR_UNSUPPORTED;
+}
+
+// Host entry of the key-list mode: q / o [Bq, H, Sq, 64], k / v
+// [B_src, H, S_src, 64] with contiguous rows, key_list [Bq, key_len] int32
+// (keys of k[key_batch[b]]), every key block live.
+int32_t bsa_fwd_sm100_keys(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
+                           const saf_tensor4* o, const int32_t* key_list, int32_t key_len,
+                           const int32_t* key_batch, float sm_scale, cudaStream_t stream) {
+  if (q->D != kD || k->D != kD) return SAF_ERR_UNSUPPORTED;
+  if (q->dtype != SAF_BF16 && q->dtype != SAF_F16) return SAF_ERR_UNSUPPORTED;
+  if (!current_device_is_sm100()) return SAF_ERR_UNSUPPORTED;
+  for (const saf_tensor4* t : {k, v})
+    if (t->stride_s != kD || t->stride_h != t->S * kD || (t->B > 1 && t->stride_b != t->H * t->S * kD))
+      return SAF_ERR_STRIDE;  // the gather reads k / v as one array of 64-element rows
+  const int64_t rows = k->B * k->H * k->S;
+  if (rows >= (int64_t(1) << 31) || key_len <= 0) return SAF_ERR_SHAPE;
+  CUtensorMap mq, mk, mv;
+  int32_t rc;
+  if ((rc = make_qkv_map(&mq, q, kBM)) != SAF_OK) return rc;
+  const CUtensorMapDataType dt =
+      q->dtype == SAF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  for (int t = 0; t < 2; ++t) {
+    const saf_tensor4* src = t == 0 ? k : v;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD * 2)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kD), 1u};  // one row: the gather4 box
+    if (encode_tensor_map(t == 0 ? &mk : &mv, dt, 2, src->data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
+        CUDA_SUCCESS)
+      return SAF_ERR_STRIDE;
+  }
+  BsaParams p{};
+  p.B = static_cast<int>(q->B);
+  p.H = static_cast<int>(q->H);
+  p.Sq = static_cast<int>(q->S);
+  p.Sk = key_len;
+  p.bm = 128;
+  p.nbq = static_cast<int>((q->S + kBM - 1) / kBM);
+  p.nbk = (key_len + 127) / 128;
+  if (p.nbk > 16384) return SAF_ERR_UNSUPPORTED;
+  p.dense = 1;
+  p.scale_log2 = sm_scale * kLog2e;
+  p.inv_scale = static_cast<float>(1.0 / static_cast<double>(sm_scale));
+  p.o = o->data;
+  p.o_sb = o->stride_b;
+  p.o_sh = o->stride_h;
+  p.o_ss = o->stride_s;
+  p.status = device_status_ptr();
+  p.budget_ns = wait_budget_ns();
+  p.key_list = key_list;
+  p.key_batch = key_batch;
+  p.key_len = key_len;
+  p.key_src_len = static_cast<int>(k->S);
+  p.key_src_batches = static_cast<int>(k->B);
+  if (p.status == nullptr) return SAF_ERR_CUDA;
+  const int n_tiles = p.nbq;
+  if (q->dtype == SAF_BF16) return launch_variant<128, false, true, kMaskKeys>(mq, mk, mv, p, n_tiles, stream);
+  return launch_variant<128, false, false, kMaskKeys>(mq, mk, mv, p, n_tiles, stream);
 }
 
 }  // namespace saf

@@ -710,3 +710,32 @@ def masked_topn(mass: torch.Tensor, local_mask: torch.Tensor, n: int) -> torch.T
                                          _stream_ptr(dev))
     _lib.check("saf_masked_topn", rc)
     return out
+
+
+def bsa_fwd_keys(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, key_list: torch.Tensor,
+                 key_batch: torch.Tensor, sm_scale: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of q ``[Bq, H, Sq, 64]`` over per-batch key lists: batch b
+    attends the rows ``key_list[b]`` (int32 ``[Bq, L]``) of
+    ``k[key_batch[b]]`` / ``v[key_batch[b]]`` (``[B_src, H, S_src, 64]``,
+    contiguous), repeated keys counted as often as listed; the rows are
+    fetched by TMA gather4 loads inside the attention kernel
+    (saf_bsa_fwd_keys)."""
+    dev = _require_cuda(q, k, v, key_list, key_batch)
+    q = _d_last(q)
+    k, v = k.contiguous(), v.contiguous()
+    if key_list.dim() != 2 or key_list.shape[0] != q.shape[0]:
+        raise ValueError(f"key_list must be [{q.shape[0]}, L]")
+    kl = key_list.to(torch.int32).contiguous()
+    kb = key_batch.to(torch.int32).contiguous()
+    if kb.numel() != q.shape[0]:
+        raise ValueError(f"key_batch must have {q.shape[0]} entries")
+    if out is None:
+        out = torch.empty_like(q)
+    tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
+    with torch.cuda.device(dev):
+        rc = _lib.load().saf_bsa_fwd_keys(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), ctypes.byref(to),
+                                          kl.data_ptr(), kl.shape[1], kb.data_ptr(), float(sm_scale),
+                                          _stream_ptr(dev))
+    _lib.check("saf_bsa_fwd_keys", rc)
+    return out
+

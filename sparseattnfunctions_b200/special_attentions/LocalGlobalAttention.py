@@ -20,9 +20,13 @@ CogVideoX-2B layer shape (226 text tokens, 13 x 30 x 45 video, B = 2):
 Here the dense rows run on the block-sparse attention kernel with every
 block live (written straight into the output rows), the probe is the
 tcgen05 probe kernel (the reference's 16-bit roundings reproduced) plus the
-masked top-n select, and the patch step gathers each (patch, batch) key
-list once (duplicates included, as the reference's torch.gather), runs the
-attention kernel over it and gathers the outputs back into token order.
+masked top-n select, and the patch step gathers the patch rows of q and
+every (patch, batch) key list of k / v once (duplicates included, as the
+reference's torch.gather), runs the attention kernel over the gathered rows
+and gathers the outputs back into token order.  With
+``gather_in_kernel=True`` the attention kernel's key-list mode fetches the
+listed k / v rows by TMA gather4 loads instead, with no gathered copy in
+HBM (less memory, but slower at this size).
 The sampled rows are drawn with the same ``torch.randint`` call as the
 reference, and the window key lists come from the same ``torch.sort`` of
 the window mask on the input's device, so both match the reference's on
@@ -173,7 +177,12 @@ class probe_solver:
 
 
 class LocalGlobalAttention:
-    def __init__(self):
+    def __init__(self, gather_in_kernel: bool = False):
+        # gather_in_kernel: attend the key lists with the rows fetched inside
+        # the attention kernel (no 2 x 0.98 GB of gathered k / v in HBM) --
+        # measured slower than gathering first at CogVideoX-2B size (4.9
+        # against 0.94 + 2.7 ms), so off by default
+        self.gather_in_kernel = gather_in_kernel
         self.compression = compression.to(dtype=torch.int32)
         self.global_indices = None
         self.padding = 0.2
@@ -245,24 +254,36 @@ class LocalGlobalAttention:
         q_idx, _ = self._patch_index(q.shape[0], q.device)
         return kernels.gather_rows(q, q_idx)
 
-    def key_lists(self, q_video, k):
-        """int64 [P*B, L]: every (patch, batch) row's key list as b*S + key."""
+    def patch_keys(self, q_video, k):
+        """(keys int32 [P*B, L], source batch int32 [P*B]): the key list of
+        every (patch, batch) row -- the window list then the probe's keys --
+        and the batch of k / v it indexes; runs the probe on the reference's
+        update_gap schedule (:221-226)."""
         global counter
         self._setup(k.device)
         if counter == 0 or self.global_indices is None:
             self.global_indices = self.probe._probe(q_video, k)
             counter = update_gap
         counter -= 1
-        B, S = k.shape[0], k.shape[2]
+        B = k.shape[0]
         n_patch = int(torch.prod(self.compression).item())
         # the window lists: row p * 2 + b of the reference's [36, remain] table
         fixed = self.indices.view(n_patch, batch_size, -1)
         fixed = fixed[:, [b if B == batch_size else 0 for b in range(B)]].reshape(n_patch * B, -1)
         lists = fixed if self.global_indices is None else torch.cat((fixed, self.global_indices), dim=-1)
-        base = (torch.arange(B, device=k.device, dtype=torch.int64) * S).repeat(n_patch).view(-1, 1)
-        return lists + base
+        src = torch.arange(B, device=k.device, dtype=torch.int32).repeat(n_patch)
+        return lists.to(torch.int32), src
+
+    def key_lists(self, q_video, k):
+        """int64 [P*B, L]: every (patch, batch) row's key list as b*S + key
+        (the flattened rows saf_gather_rows reads)."""
+        keys, src = self.patch_keys(q_video, k)
+        return keys.to(torch.int64) + src.to(torch.int64).view(-1, 1) * k.shape[2]
 
     def transform_kv_v1(self, q, k, v):
+        """The gathered k / v of every (patch, batch) list, as the reference
+        builds them (the forward does not materialise them: the attention
+        kernel reads the listed rows in place)."""
         idx = self.key_lists(q, k)
         return kernels.gather_rows(k, idx), kernels.gather_rows(v, idx)
 
@@ -283,9 +304,13 @@ class LocalGlobalAttention:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
         dense = TEXT_LEN + Hh * W
         self.attention_text(self.slice_text(q), k, v, out=out[:, :, :dense])
-        kp, vp = self.transform_kv_v1(self.slice_video(q), k, v)
         qp = self.transform_q(q)
-        op = self.attention_video(qp, kp, vp)
+        if self.gather_in_kernel:
+            keys, src = self.patch_keys(self.slice_video(q), k)
+            op = kernels.bsa_fwd_keys(qp, k, v, keys, src, 1.0 / math.sqrt(D))
+        else:
+            kp, vp = self.transform_kv_v1(self.slice_video(q), k, v)
+            op = self.attention_video(qp, kp, vp)
         self.transform_output(op, out=out[:, :, dense:])
         return out
 

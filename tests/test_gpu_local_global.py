@@ -12,6 +12,9 @@ tests/golden/local_global.npz).
   boundary); an f16 case with ragged row and key counts against the oracle.
 * saf_masked_topn: bit-exact against the oracle's stable top-n, on the
   probe mass and on a tie-heavy integer mass.
+* saf_bsa_fwd_keys (attention over per-batch key lists, rows fetched by TMA
+  gather4 loads): within 2e-2 of the fp64 oracle, repeated keys and ragged
+  lists included; an out-of-range key sets the bad-index flag.
 * The processor at CogVideoX-2B size (B=2, H=30, bf16): window lists, the
   probe's keys (the stable top-n of its own mass), sampled output rows of
   the dense part and of both patch groups within 2e-2 of the fp64 oracle
@@ -64,6 +67,39 @@ def test_gather_rows_bad_index_sets_flag(cuda_device):
     got = kernels.gather_rows(x, idx)
     torch.cuda.synchronize()
     assert bool((got[:, :, 1] == 0).all()) and bool((got[:, :, [0, 2]] == 1).all())
+    assert _lib.read_device_status(0, clear=True) & _lib.SAF_DEV_BADINDEX
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_key_list_attention_matches_oracle(cuda_device, dtype):
+    """saf_bsa_fwd_keys: every query batch attends its own list of rows of
+    one k / v batch (gather4 loads), repeated keys counted twice, a ragged
+    last block of the list and a ragged query tile."""
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn(3, 2, 200, 64, generator=g).to(dtype)
+    k = torch.randn(2, 2, 500, 64, generator=g).to(dtype)
+    v = torch.randn(2, 2, 500, 64, generator=g).to(dtype)
+    keys = torch.randint(0, 500, (3, 300), generator=g, dtype=torch.int32)
+    keys[0, :10] = 7  # repeats
+    src = torch.tensor([1, 0, 1], dtype=torch.int32)
+    out = kernels.bsa_fwd_keys(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), keys.to(cuda_device),
+                               src.to(cuda_device), 0.125).cpu()
+    for b in range(3):
+        kb, vb = k[src[b].item()][None], v[src[b].item()][None]
+        rows = [(0, t) for t in range(200)]
+        ref = olg.attention_rows(q[b][None], kb, vb, rows, lambda _b, _t: keys[b].numpy().astype(np.int64))
+        assert np.abs(out[b].permute(1, 0, 2).float().numpy() - ref).max() < 2e-2
+
+
+@pytest.mark.expects_device_status
+def test_key_list_bad_index_sets_flag(cuda_device):
+    _lib.read_device_status(0, clear=True)
+    q = torch.randn(1, 1, 128, 64, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(1, 1, 256, 64, device=cuda_device).to(torch.bfloat16)
+    keys = torch.arange(128, dtype=torch.int32, device=cuda_device).view(1, -1)
+    keys[0, 5] = 256  # past the rows of k
+    kernels.bsa_fwd_keys(q, k, k, keys, torch.zeros(1, dtype=torch.int32, device=cuda_device), 0.125)
+    torch.cuda.synchronize()
     assert _lib.read_device_status(0, clear=True) & _lib.SAF_DEV_BADINDEX
 
 
@@ -169,6 +205,21 @@ def test_output_rows_match_oracle(full_run):
     ref = olg.attention_rows(q.cpu(), k.cpu(), v.cpu(), rows, keys_of)
     got = np.stack([out[b, :, t].float().cpu().numpy() for b, t in rows])
     assert np.abs(got - ref).max() < 2e-2
+
+
+def test_key_lists_in_kernel_equal_gathered_copies(full_run):
+    """The processor's two patch paths -- attention over gathered k / v
+    copies, and the kernel's key-list mode fetching the same rows by gather4
+    -- read the same values in the same block order: identical outputs."""
+    q, k, v, obj, out, samples = full_run
+    lga.counter = 1 << 20  # keep the probe keys of the first call
+    obj.gather_in_kernel = True
+    try:
+        out_keys = obj(q, k, v)
+    finally:
+        obj.gather_in_kernel = False
+        lga.counter = lga.update_gap - 1
+    assert torch.equal(out_keys, out)
 
 
 def test_probe_update_gap(full_run, cuda_device):

@@ -427,32 +427,66 @@ struct GatherParams {
   unsigned int* status;
 };
 
+// Four gathered rows per warp (independent loads in flight); each row's
+// squared norm keeps the contract's order (lane l: columns l, l + 32, ...
+// ascending, then the xor butterfly).
+constexpr int kGatherRows = 4;
+
 template <typename T>
 __global__ void __launch_bounds__(256) tome_gather_kernel(const GatherParams g) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y;
-  if (warp >= g.n_rows) return;
-  int tok = g.idx[warp];
-  T* dst = static_cast<T*>(g.out) + (static_cast<int64_t>(b) * g.n_rows + warp) * g.Cp;
-  if (tok < 0 || tok >= g.N) {
-    if (lane == 0) atomicOr(g.status, SAF_DEV_BADINDEX);
-    tok = -1;
+  const int r0 = w * kGatherRows;
+  if (r0 >= g.n_rows) return;
+  const T* src[kGatherRows];
+  T* dst[kGatherRows];
+  bool ok[kGatherRows];
+  double acc[kGatherRows];
+#pragma unroll
+  for (int r = 0; r < kGatherRows; ++r) {
+    const int row = min(r0 + r, g.n_rows - 1);
+    int tok = g.idx[row];
+    if (tok < 0 || tok >= g.N) {
+      if (lane == 0 && r0 + r < g.n_rows) atomicOr(g.status, SAF_DEV_BADINDEX);
+      tok = -1;
+    }
+    ok[r] = tok >= 0;
+    src[r] = static_cast<const T*>(g.metric) + static_cast<int64_t>(b) * g.sb +
+             static_cast<int64_t>(tok < 0 ? 0 : tok) * g.sn;
+    dst[r] = static_cast<T*>(g.out) + (static_cast<int64_t>(b) * g.n_rows + row) * g.Cp;
+    acc[r] = 0.0;
   }
-  const T* src = static_cast<const T*>(g.metric) + static_cast<int64_t>(b) * g.sb +
-                 static_cast<int64_t>(tok < 0 ? 0 : tok) * g.sn;
-  double acc = 0.0;
-  for (int c = lane; c < g.Cp; c += 32) {
-    T v = T(0.f);
-    if (c < g.C && tok >= 0) v = src[c];
-    dst[c] = v;
-    const double d = ld_f64(&v);
-    acc = fma(d, d, acc);  // products of 16-bit values are exact in fp64
+  // two columns per lane and row loaded before any store (eight loads in flight)
+  for (int c0 = lane; c0 < g.Cp; c0 += 64) {
+    T v[2][kGatherRows];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = c0 + 32 * u;
+#pragma unroll
+      for (int r = 0; r < kGatherRows; ++r) v[u][r] = (c < g.C && ok[r]) ? src[r][c] : T(0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = c0 + 32 * u;
+      if (c >= g.Cp) break;
+#pragma unroll
+      for (int r = 0; r < kGatherRows; ++r) {
+        if (r0 + r < g.n_rows) dst[r][c] = v[u][r];
+        const double d = ld_f64(&v[u][r]);
+        acc[r] = fma(d, d, acc[r]);  // products of 16-bit values are exact in fp64
+      }
+    }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
-    g.sqnorm[static_cast<int64_t>(b) * g.n_rows + warp] = acc;
-    if (g.rinv) g.rinv[static_cast<int64_t>(b) * ((g.n_rows + 3) & ~3) + warp] = static_cast<float>(1.0 / sqrt(acc));
+  for (int r = 0; r < kGatherRows; ++r) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+    const int row = r0 + r;
+    if (lane == 0 && row < g.n_rows) {
+      g.sqnorm[static_cast<int64_t>(b) * g.n_rows + row] = acc[r];
+      if (g.rinv)
+        g.rinv[static_cast<int64_t>(b) * ((g.n_rows + 3) & ~3) + row] = static_cast<float>(1.0 / sqrt(acc[r]));
+    }
   }
 }
 
@@ -470,10 +504,23 @@ struct ExactParams {
   int32_t* node_idx;    // [B, Ns]
 };
 
+// Eight columns per lane are loaded before they are summed, so a lane has
+// 16 loads in flight instead of two (a zero pad past Cp adds +0 and leaves
+// every partial sum unchanged).
 template <typename T>
 __device__ __forceinline__ double exact_dot(const T* a, const T* bb, int Cp, int lane) {
   double acc = 0.0;
-  for (int c = lane; c < Cp; c += 32) acc = fma(ld_f64(a + c), ld_f64(bb + c), acc);
+  for (int c0 = lane; c0 < Cp; c0 += 32 * 8) {
+    double av[8], bv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = c0 + 32 * i;
+      av[i] = c < Cp ? ld_f64(a + c) : 0.0;
+      bv[i] = c < Cp ? ld_f64(bb + c) : 0.0;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fma(av[i], bv[i], acc);
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   return acc;  // the contract's summation order (see the file header)
@@ -963,14 +1010,14 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   GatherParams g{metric, stride_b, stride_n, static_cast<int>(B), static_cast<int>(N),
                  static_cast<int>(C), static_cast<int>(Cp), a_idx, static_cast<int>(Ns), A, na,
                  nullptr, status};
-  dim3 gg_a(static_cast<unsigned>((Ns + 7) / 8), static_cast<unsigned>(B));
+  dim3 gg_a(static_cast<unsigned>((Ns + 8 * kGatherRows - 1) / (8 * kGatherRows)), static_cast<unsigned>(B));
   GatherParams gb = g;
   gb.idx = b_idx;
   gb.n_rows = static_cast<int>(Nd);
   gb.out = Bm;
   gb.sqnorm = nb;
   gb.rinv = rinv;
-  dim3 gg_b(static_cast<unsigned>((Nd + 7) / 8), static_cast<unsigned>(B));
+  dim3 gg_b(static_cast<unsigned>((Nd + 8 * kGatherRows - 1) / (8 * kGatherRows)), static_cast<unsigned>(B));
   if (bf16) {
     tome_gather_kernel<__nv_bfloat16><<<gg_a, 256, 0, st>>>(g);
     tome_gather_kernel<__nv_bfloat16><<<gg_b, 256, 0, st>>>(gb);
@@ -1005,8 +1052,9 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   // 3. exact fp64 re-score of the candidates
   ExactParams ep{A, Bm, na, nb, ci, cv, static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd),
                  static_cast<int>(Cp), nmax, nidx};
-  if (bf16) tome_exact_kernel<__nv_bfloat16><<<gg_a, 256, 0, st>>>(ep);
-  else tome_exact_kernel<__half><<<gg_a, 256, 0, st>>>(ep);
+  dim3 ge(static_cast<unsigned>((Ns + 7) / 8), static_cast<unsigned>(B));
+  if (bf16) tome_exact_kernel<__nv_bfloat16><<<ge, 256, 0, st>>>(ep);
+  else tome_exact_kernel<__half><<<ge, 256, 0, st>>>(ep);
   SAF_CUDA_TRY(cudaGetLastError());
 
   // 4. stable sort of node_max (descending) per batch row

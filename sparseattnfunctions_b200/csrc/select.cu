@@ -163,13 +163,14 @@ __device__ __forceinline__ bool better(double a, int ia, double b, int ib) {
   return a > b || (a == b && ia < ib);
 }
 
-// grid (B*H, ceil(nbq / 32)), 256 threads; each warp owns kRowsPerWarp
+// grid (B*H, ceil(nbq / 16)), 256 threads; each warp owns kRowsPerWarp
 // consecutive row blocks, so every key mean staged in shared memory (32 dims
-// at a time) serves four rows.  Every lane owns columns lane + 32m (m < M)
+// at a time) serves two rows (two rather than four: twice the CTAs, and the
+// serial top-k rounds of a warp cover half the rows).  Every lane owns columns lane + 32m (m < M)
 // and accumulates their fp64 scores with d ascending (separate multiply and
 // add, no contraction).  The top-k is k rounds of a warp arg-max (ties ->
 // lower column).
-constexpr int kRowsPerWarp = 4;
+constexpr int kRowsPerWarp = 2;
 constexpr int kRowsPerCta = 8 * kRowsPerWarp;
 
 template <int M>

@@ -264,8 +264,12 @@ int32_t saf_bsa_fwd_frames(const saf_tensor4* q, const saf_tensor4* k, const saf
  * R[r, j] = row r's largest logit in key block j (log2 units, sm_scale
  * folded in; -inf for blocks the row does not visit), lse_r = the row's
  * log2-sum-exp; then every row of pool_out is divided by its sum.
+ * pool_block is 128, or 64 with 64-row mask blocks (block_m 64): a pooled
+ * row is one 128-row query tile of the kernel or one half of it, reduced in
+ * the tile's epilogue (no pass over an R array in HBM).
  * workspace: caller-allocated, at least saf_bsa_pool_workspace_bytes(B*H,
- * Sq, nbk) bytes (R and lse in fp32).  fp32 inputs: SAF_ERR_UNSUPPORTED.
+ * Sq, nbk) bytes (each persistent CTA's R of its current tile, fp32; sized
+ * for the current device).  fp32 inputs: SAF_ERR_UNSUPPORTED.
  * Replaces: attn_with_pooling / _attention_pooling.forward and _attn_fwd
  * (special_attentions/utils/attn_pooling_kernel.py:25-97,106-264; the
  * non-causal case, whose query and key blocks are both block_size). */

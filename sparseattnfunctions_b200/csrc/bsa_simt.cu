@@ -16,7 +16,7 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
                       int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
-                      const FrameMaskArgs* frames, float* pool_rmax, float* pool_lse,
+                      const FrameMaskArgs* frames, const PoolArgs* pool,
                       cudaStream_t stream);
 int32_t bsa_fwd_sm100_keys(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
                            const saf_tensor4* o, const int32_t* key_list, int32_t key_len,
@@ -263,14 +263,14 @@ int32_t check_operand(const saf_tensor4* t, const saf_tensor4* ref) {
 
 using namespace saf;
 
-// Validation and dispatch shared by the attention entry points; pool_rmax /
-// pool_lse (16-bit path only) receive the pooled-map statistics.
+// Validation and dispatch shared by the attention entry points; `pool`
+// (16-bit path only) asks for the pooled attention map.
 int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int32_t block_m, int32_t block_n, const float* kv_bias,
                       int64_t kv_bias_stride_bh, float sm_scale, int32_t lead_rows,
-                      const int32_t* row_ranges, const FrameMaskArgs* frames, float* pool_rmax,
-                      float* pool_lse, void* stream) {
+                      const int32_t* row_ranges, const FrameMaskArgs* frames, const PoolArgs* pool,
+                      void* stream) {
   int32_t rc = check_tensor4(q);
   if (rc != SAF_OK) return rc;
   if ((rc = check_operand(k, q)) != SAF_OK) return rc;
@@ -285,7 +285,7 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   if (row_ranges != nullptr && (reinterpret_cast<uintptr_t>(row_ranges) & 15) != 0) return SAF_ERR_STRIDE;
   if (row_ranges != nullptr && kv_bias != nullptr) return SAF_ERR_UNSUPPORTED;
   if (frames != nullptr) {
-    if (row_ranges != nullptr || kv_bias != nullptr || pool_rmax != nullptr) return SAF_ERR_UNSUPPORTED;
+    if (row_ranges != nullptr || kv_bias != nullptr || pool != nullptr) return SAF_ERR_UNSUPPORTED;
     if (frames->bits == nullptr) return SAF_ERR_ARG;
     if (frames->frames < 1 || frames->frames > 32 || frames->text_len < 0 || frames->frame_len < block_n ||
         q->S != k->S ||
@@ -295,7 +295,7 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (q->dtype == SAF_F32) {
-    if (pool_rmax != nullptr || pool_lse != nullptr) return SAF_ERR_UNSUPPORTED;
+    if (pool != nullptr) return SAF_ERR_UNSUPPORTED;
     DeviceScope dev_scope;
     if ((rc = dev_scope.bind(q->data)) != SAF_OK) return rc;
     return bsa_fwd_simt(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
@@ -318,7 +318,7 @@ int32_t bsa_fwd_entry(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   return bsa_fwd_sm100(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
                        kv_bias_stride_bh, sm_scale,
                        static_cast<int>(lead_tiles < 65535 ? lead_tiles : 65535), row_ranges,
-                       frames, pool_rmax, pool_lse, st);
+                       frames, pool, st);
 }
 
 extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k,
@@ -329,8 +329,7 @@ extern "C" int32_t saf_bsa_fwd_ranges(const saf_tensor4* q, const saf_tensor4* k
                                       float sm_scale, int32_t lead_rows, const int32_t* row_ranges,
                                       void* stream) {
   return bsa_fwd_entry(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, kv_bias,
-                       kv_bias_stride_bh, sm_scale, lead_rows, row_ranges, nullptr, nullptr, nullptr,
-                       stream);
+                       kv_bias_stride_bh, sm_scale, lead_rows, row_ranges, nullptr, nullptr, stream);
 }
 
 extern "C" int32_t saf_bsa_fwd_frames(const saf_tensor4* q, const saf_tensor4* k,
@@ -342,7 +341,7 @@ extern "C" int32_t saf_bsa_fwd_frames(const saf_tensor4* q, const saf_tensor4* k
                                       void* stream) {
   const FrameMaskArgs fm{frame_bits, text_len, frame_len, frames};
   return bsa_fwd_entry(q, k, v, o, row_ptr, col_idx, col_capacity, block_m, block_n, nullptr, 0,
-                       sm_scale, lead_rows, nullptr, &fm, nullptr, nullptr, stream);
+                       sm_scale, lead_rows, nullptr, &fm, nullptr, stream);
 }
 
 extern "C" int32_t saf_bsa_fwd(const saf_tensor4* q, const saf_tensor4* k, const saf_tensor4* v,

@@ -67,6 +67,9 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128, kColP = 192;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+#ifndef SAF_OVERFLOW_GUARD
+#define SAF_OVERFLOW_GUARD 1
+#endif
 
 struct BsaParams {
   int B, H, Sq, Sk;
@@ -95,8 +98,9 @@ struct BsaParams {
   // nullable pooled-map outputs (attention with pooling): per visited key
   // block the row's maximum logit in log2 units, [B*H, nbk, Sq], and the
   // row's log2-sum-exp, [B*H, Sq]
-  float* pool_rmax;
-  float* pool_lse;
+  float* pool_scratch;  // [grid][2][list_cap][128] block maxima of each CTA's last two tiles
+  float* pool_out;      // [B*H, nbp, nbk], zeroed: per-row block maxima pooled by atomic max
+  int pool_block, nbp;
   // persistent schedule: query tiles per head, heads, and this launch's
   // [next tile, CTAs done] counters (zero on entry; the last CTA resets them)
   int n_tiles, BH;
@@ -252,8 +256,8 @@ struct Layout {
   static constexpr int kOffBar = kOffOnes + (kBias ? kBM * 32 : 0);
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
   //           b_full[VS], s_full, s_empty, p_full, pv_full, drain, b_empty[VS],
-  //           q_empty, tile_full[2], tile_empty[2]
-  static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 10;
+  //           q_empty, tile_full[2], tile_empty[2], pool_full[2], pool_empty[2]
+  static constexpr int kNumBars = 1 + 2 * kKS + 4 * kVS + 14;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   // tile lists (runtime size, after the fixed part): 2 slots of list_cap
   // uint16 entries, then two bitmaps of the key blocks
@@ -261,13 +265,17 @@ struct Layout {
   static constexpr int kBytes = kOffList;
   static constexpr int kDynSmem = kBytes + 1024;  // slack for 1024B alignment
 };
-inline int list_smem_bytes(int list_cap, int nbk) { return 2 * list_cap * 2 + 2 * ((nbk + 31) / 32) * 4; }
+inline int list_smem_bytes(int list_cap, int nbk) {
+  return 2 * list_cap * 2 + 2 * ((nbk + 31) / 32) * 4 + 2 * 128 * 4;  // lists, bitmaps, pooled-map lse
+}
 
 // Masks applied inside a visited block, besides the ragged tail: none, the
 // per-row key intervals of row_ranges, or the per-head frame masks.
 constexpr int kMaskNone = 0, kMaskRanges = 1, kMaskFrames = 2;
 // Key-list mode (no mask besides the ragged tail; K / V rows by gather4).
 constexpr int kMaskKeys = 3;
+// Attention with a pooled map (no mask besides the ragged tail).
+constexpr int kMaskPool = 4;
 
 // TMA gather4: four rows (coordinates r0..r3 of a 2-D map whose box is one
 // row of 64 elements) into 4 x 128 bytes of shared memory, 128-byte swizzle
@@ -334,12 +342,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_q_empty = bar0 + 8u * (1 + 2 * kKS + 4 * kVS + 5);
   auto bar_tile_full = [&](int s) { return bar_q_empty + 8u * (1 + s); };
   auto bar_tile_empty = [&](int s) { return bar_q_empty + 8u * (3 + s); };
+  // attention with a pooled map: the softmax warps hand each tile's block
+  // maxima (in the scratch slot of the tile's parity) and the rows'
+  // log2-sum-exp to warps 2-3, which pool them while the next tile runs
+  auto bar_pool_full = [&](int s) { return bar_q_empty + 8u * (5 + s); };
+  auto bar_pool_empty = [&](int s) { return bar_q_empty + 8u * (7 + s); };
+  constexpr bool kPool = kMask == kMaskPool;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   volatile int* tile_slot = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);  // [2]
   volatile int* tile_cnt = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 16);  // [2] list lengths
   uint16_t* list_base = reinterpret_cast<uint16_t*>(smem + L::kOffList);            // [2][list_cap]
   uint32_t* list_bits = reinterpret_cast<uint32_t*>(smem + L::kOffList + 4 * p.list_cap);
+  float* pool_lse = reinterpret_cast<float*>(list_bits + 2 * ((p.nbk + 31) / 32));  // [2][128]
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
@@ -361,7 +376,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(bar_q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar_tile_full(s), 1);
-      mbar_init(bar_tile_empty(s), 1 + 128);  // the MMA thread and the softmax threads
+      // the MMA thread, the softmax threads and, pooling, warps 2-3
+      mbar_init(bar_tile_empty(s), 1 + 128 + (kPool ? 64 : 0));
+      mbar_init(bar_pool_full(s), 128);
+      mbar_init(bar_pool_empty(s), 64);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -622,6 +640,64 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_commit(bar_drain);
       mbar_drain(bar_drain, 0, p.status);
     }
+    } else if (kPool) {
+    // ------------------------------------------------------------ pool reducer
+    // Warps 2-3 (attention with a pooled map): for every tile, per listed
+    // key block, exp2(R - lse) of each row, the maximum over a pool row
+    // pooled into the map by an atomic max (non-negative floats order as
+    // integers).  Thread t takes rows t and t + 64.
+    const int t = threadIdx.x - 64;
+    int ti = 0;
+    while (true) {
+      const int slot = ti & 1;
+      const uint32_t par = (ti >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_tile_full(slot), par, abort_flag, p.status, p.budget_ns))) break;
+      const int lin = tile_slot[slot];
+      const int n_blk = tile_cnt[slot];
+      ++ti;
+      if (lin >= n_total) {
+        mbar_arrive(bar_tile_empty(slot));
+        break;
+      }
+      int tile, g;
+      tile_of(lin, tile, g);
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_pool_full(slot), par, abort_flag, p.status, p.budget_ns))) break;
+      const float lse0 = pool_lse[slot * kBM + t], lse1 = pool_lse[slot * kBM + t + 64];
+      const float* scr = p.pool_scratch + (static_cast<int64_t>(blockIdx.x) * 2 + slot) * p.list_cap * kBM;
+      const uint16_t* lst = list_base + slot * p.list_cap;
+      const int pr0 = tile * kBM / p.pool_block;
+      int* po = reinterpret_cast<int*>(p.pool_out) + static_cast<int64_t>(g) * p.nbp * p.nbk;
+      for (int j0 = 0; j0 < n_blk; j0 += 8) {
+        float r0[8], r1[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int jj = j0 + u < n_blk ? j0 + u : n_blk - 1;
+          r0[u] = scr[jj * kBM + t];
+          r1[u] = scr[jj * kBM + t + 64];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int jj = j0 + u;
+          const float e0 = lse0 == -INFINITY ? 0.f : exp2f(r0[u] - lse0);
+          const float e1 = lse1 == -INFINITY ? 0.f : exp2f(r1[u] - lse1);
+          const int col = lst[jj < n_blk ? jj : 0] & 0x3fff;
+          if (p.pool_block == kBM) {
+            const uint32_t w = __reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(e0, e1)));
+            if (lane == 0 && jj < n_blk && pr0 < p.nbp)
+              atomicMax(po + static_cast<int64_t>(pr0) * p.nbk + col, static_cast<int>(w));
+          } else {  // two pool rows of 64 per tile: rows t (first) and t + 64 (second)
+            const uint32_t w0 = __reduce_max_sync(0xffffffffu, __float_as_uint(e0));
+            const uint32_t w1 = __reduce_max_sync(0xffffffffu, __float_as_uint(e1));
+            if (lane == 0 && jj < n_blk) {
+              if (pr0 < p.nbp) atomicMax(po + static_cast<int64_t>(pr0) * p.nbk + col, static_cast<int>(w0));
+              if (pr0 + 1 < p.nbp) atomicMax(po + static_cast<int64_t>(pr0 + 1) * p.nbk + col, static_cast<int>(w1));
+            }
+          }
+        }
+      }
+      mbar_arrive(bar_pool_empty(slot));
+      mbar_arrive(bar_tile_empty(slot));
+    }
     }
     // ------------------------------------------------------------ teardown
     __syncwarp();
@@ -690,6 +766,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     const uint16_t* lst = list_base + slot * p.list_cap;
+    if constexpr (kPool) {
+      // this parity's scratch slot is free once the reducer pooled the tile
+      // two tiles back
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_pool_empty(slot), (((ti - 1) >> 1) & 1) ^ 1, abort_flag,
+                                              p.status, p.budget_ns))) {
+        ok = false;
+        break;
+      }
+    }
     int j = 0;  // blocks of this tile
     while (j < n_blk) {
       const uint32_t ent = lst[j];
@@ -778,11 +863,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       // P = exp2(logit - m) in the input type, row sum in fp32 pairs, 32
       // scores at a time (the empty asm after each store keeps the next part's
       // exp2 from being scheduled early, bounding live registers).
-      // keep: 0 zeroes P of a row with no live score yet (the polynomial maps
+      // zero: P of a row with no live score yet is 0 (the polynomial maps
       // -inf to 2^-126, not 0), keeping such rows at l = 0 as the reference.
-      auto exp_pass = [&](float neg_m, bool with_max, float keep) -> bool {
+      auto exp_pass = [&](float neg_m, bool with_max, bool zero) -> bool {
         const f2 negm2 = mk2(neg_m, neg_m);
-        const f2 keep2 = mk2(keep, keep);
         rs = mk2(0.f, 0.f);
         float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -803,10 +887,9 @@ __global__ void __launch_bounds__(kThreads, 2)
               e0 = ex2_approx(lo2(x));
               e1 = ex2_approx(hi2(x));
             }
-            if (!with_max) {
-              const f2 z = mul2(mk2(e0, e1), keep2);
-              e0 = lo2(z);
-              e1 = hi2(z);
+            if (zero) {
+              e0 = 0.f;
+              e1 = 0.f;
             }
             rs = add2(rs, mk2(e0, e1));
             pk[e] = kBF16 ? pack_bf16x2(e0, e1) : pack_f16x2(e0, e1);
@@ -823,27 +906,46 @@ __global__ void __launch_bounds__(kThreads, 2)
         return true;
       };
 
+      auto block_max = [&]() {
+        float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < BN / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
+        return fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
+      };
+#if SAF_OVERFLOW_GUARD
+      // Speculative P with the running max, no block maximum: the max moves
+      // only for a row whose block sum shows P could approach overflow
+      // (> 2^64; the normalised result does not depend on which max P was
+      // taken against).  The pooled map needs every block's maximum, so that
+      // mode keeps the threshold rule below.
+      constexpr bool kGuard = kMask != kMaskPool;
+#else
+      constexpr bool kGuard = false;
+#endif
       if (spec) {
-        if (!exp_pass(-m_run, true, 1.f)) {
+        if (!exp_pass(-m_run, !kGuard, false)) {
           ok = false;
           break;
         }
       } else {
-        float acc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int i = 0; i < BN / 2; ++i) acc[i & 3] = fmax3(acc[i & 3], t[2 * i], t[2 * i + 1]);
-        mx = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
+        mx = block_max();
       }
-      mx *= sl2;
-      if (p.pool_rmax != nullptr && q0 + row < p.Sq)
-        p.pool_rmax[(static_cast<int64_t>(g) * p.nbk + col) * p.Sq + q0 + row] = mx;
-      const bool upd = mx > m_run + kRescaleThreshold;
+      bool upd;
+      if (kGuard && spec) {
+        upd = !(lo2(rs) + hi2(rs) <= 1.8446744e19f);  // 2^64; catches inf and NaN too
+        if (__any_sync(0xffffffffu, upd)) mx = block_max() * sl2;
+      } else {
+        mx *= sl2;
+        upd = mx > m_run + kRescaleThreshold;
+      }
+      if constexpr (kPool)
+        p.pool_scratch[((static_cast<int64_t>(blockIdx.x) * 2 + slot) * p.list_cap + j) * kBM + row] = mx;
       const float m_new = upd ? mx : m_run;
       const float alpha = upd ? ex2_approx(m_run - m_new) : 1.f;
       const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
       const bool any_upd = __any_sync(0xffffffffu, upd);
       if (!spec || any_upd) {
-        if (!exp_pass(neg_m, false, m_new == -INFINITY ? 0.f : 1.f)) {
+        if (!exp_pass(neg_m, false, m_new == -INFINITY)) {
           ok = false;
           break;
         }
@@ -870,9 +972,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(bar_p_full);
       ++j;
     }
-    // the tile's block list is no longer read: the producer may refill the slot
-    mbar_arrive(bar_tile_empty(slot));
-
     // ---------------------------------------------------------- epilogue
     // O is read back 32 columns at a time, normalised by 1/l and stored.  A
     // zero row sum gives 0 * inf = NaN, matching the reference; a tile with no
@@ -884,8 +983,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (have_o) tc_fence_after();
     const int qrow = q0 + row;
     const float inv_l = 1.f / l_run;
-    if (p.pool_lse != nullptr && qrow < p.Sq)
-      p.pool_lse[static_cast<int64_t>(g) * p.Sq + qrow] = m_run + log2f(l_run);
+    if constexpr (kPool) {
+      // hand the tile's row statistics to the pool reducer (warps 2-3); a
+      // row past Sq or with no visible key pools nothing
+      pool_lse[slot * kBM + row] = (ok && qrow < p.Sq && l_run > 0.f) ? m_run + log2f(l_run) : -INFINITY;
+      mbar_arrive(bar_pool_full(slot));
+    }
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
                    2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
                         static_cast<int64_t>(qrow) * p.o_ss);
@@ -915,6 +1018,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
+    // the tile's block list is no longer read: the producer may refill the slot
+    mbar_arrive(bar_tile_empty(slot));
     jbase += j;
     }  // tile loop
     tc_fence_before();
@@ -989,7 +1094,7 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
                       const saf_tensor4* o, const int32_t* row_ptr, const int32_t* col_idx,
                       int64_t col_capacity, int bm, int bn, const float* kv_bias,
                       int64_t bias_stride, float sm_scale, int lead_tiles, const int32_t* row_ranges,
-                      const FrameMaskArgs* frames, float* pool_rmax, float* pool_lse,
+                      const FrameMaskArgs* frames, const PoolArgs* pool,
                       cudaStream_t stream) {
   if (q->D != kD) return SAF_ERR_UNSUPPORTED;
   if (frames != nullptr && (row_ranges != nullptr || kv_bias != nullptr)) return SAF_ERR_UNSUPPORTED;
@@ -1030,13 +1135,21 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
     p.frame_len = frames->frame_len;
     p.frames = frames->frames;
   }
-  p.pool_rmax = pool_rmax;
-  p.pool_lse = pool_lse;
+  if (pool != nullptr) {
+    p.pool_scratch = pool->scratch;
+    p.pool_out = pool->out;
+    p.pool_block = pool->pool_block;
+    p.nbp = static_cast<int>((q->S + pool->pool_block - 1) / pool->pool_block);
+  }
   if (p.status == nullptr) return SAF_ERR_CUDA;
   const int n_tiles = static_cast<int>((q->S + kBM - 1) / kBM);
   const bool bf16 = q->dtype == SAF_BF16;
   const bool bias = kv_bias != nullptr;
-  const int mask = frames != nullptr ? kMaskFrames : (row_ranges != nullptr ? kMaskRanges : kMaskNone);
+  const int mask = frames != nullptr ? kMaskFrames
+                   : row_ranges != nullptr ? kMaskRanges
+                   : pool != nullptr       ? kMaskPool
+                                           : kMaskNone;
+  if (pool != nullptr && (bias || frames != nullptr || row_ranges != nullptr)) return SAF_ERR_UNSUPPORTED;
 #define SAF_BSA_CASE(BN_, BIAS_, BF_, MASK_)                               \
   if (bn == BN_ && bias == BIAS_ && bf16 == BF_ && mask == MASK_)          \
     return launch_variant<BN_, BIAS_, BF_, MASK_>(mq, mk, mv, p, n_tiles, stream);
@@ -1056,6 +1169,10 @@ int32_t bsa_fwd_sm100(const saf_tensor4* q, const saf_tensor4* k, const saf_tens
   SAF_BSA_CASE(128, false, false, kMaskFrames)
   SAF_BSA_CASE(64, false, true, kMaskFrames)
   SAF_BSA_CASE(64, false, false, kMaskFrames)
+  SAF_BSA_CASE(128, false, true, kMaskPool)
+  SAF_BSA_CASE(128, false, false, kMaskPool)
+  SAF_BSA_CASE(64, false, true, kMaskPool)
+  SAF_BSA_CASE(64, false, false, kMaskPool)
 #undef SAF_BSA_CASE
   return SAF_ERR_UNSUPPORTED;
 }

@@ -62,6 +62,16 @@ struct FrameMaskArgs {
   int32_t text_len, frame_len, frames;
 };
 
+// Pooled attention map of the 16-bit attention kernel (attention with
+// pooling): `out` [B*H, ceil(Sq / pool_block), nbk] fp32, zeroed by the
+// caller (key blocks a pool row never visits stay 0); `scratch` holds each
+// persistent CTA's block maxima of its current tile (pool_scratch_floats()).
+struct PoolArgs {
+  float* scratch;
+  float* out;
+  int32_t pool_block;  // 64 or 128 query rows per pooled row
+};
+
 // Common checks of a [B,H,S,D] view: non-null, D-stride 1 implied, positive
 // sizes, known dtype.
 inline int32_t check_tensor4(const saf_tensor4* t) {

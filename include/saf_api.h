@@ -177,7 +177,12 @@ int32_t saf_topk_adaptive_select(const double* in, int32_t is_mass, int64_t BH, 
  * lead_rows: query blocks [0, lead_rows) of every head are scheduled before
  * all others -- pass the number of dense (text) rows, whose block lists are
  * the longest, so they do not start last and stretch the tail; 0 keeps
- * head-major order.  Results do not depend on it.
+ * head-major order.  With few heads per GPU a lead tile would outlast the
+ * rest of the launch, so their key blocks are split over up to 8 work items
+ * whose partial rows are merged by the last of them (fp32 partials in a
+ * static 16 MiB per-device buffer: launches with lead_rows > 0 on one
+ * device must not overlap; launches whose partials would not fit run
+ * unsplit).  Results do not depend on it beyond fp32 rounding.
  * Each launch takes one of 64 per-device tile-counter slots, round-robin
  * at launch time, and leaves it at zero when it ends: launches ordered on
  * one stream, or fewer than 64 in flight at once, never share a live slot.

@@ -67,6 +67,9 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128, kColP = 192;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// a split partial row: O (64 fp32), m, l, padded to 16-byte multiples so
+// every row starts 16-byte aligned for the vector stores and loads
+constexpr int kSplitRow = kD + 4;
 #ifndef SAF_OVERFLOW_GUARD
 #define SAF_OVERFLOW_GUARD 1
 #endif
@@ -87,6 +90,12 @@ struct BsaParams {
   unsigned int* status;
   uint64_t budget_ns;
   int lead_tiles;  // query tiles per head scheduled first
+  // split key ranges of the lead tiles: each lead tile's block list is cut
+  // into `splits` work items whose unnormalised partial results (O, m, l per
+  // row) go to split_part; the last item of a row to finish merges them
+  int splits;         // the most work items a lead tile may be split into (1: none)
+  float* split_part;  // [B*H, lead_tiles, splits, 128, kSplitRow], 16-byte aligned rows
+  int* split_cnt;     // [B*H, lead_tiles, 128], zero on entry
   // nullable [Sq] int4: the key columns of query row r are limited to
   // [x, y) U [z, w) (frame-band masks); shared by every head
   const int4* row_ranges;
@@ -308,18 +317,45 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Tile order: the first `lead_tiles` query tiles of every head (dense text
   // rows, the longest block lists) first, tile-major; the rest head-major so
   // that CTAs working at the same time share a head's K/V in L2.
-  const int n_total = p.n_tiles * p.BH;
-  auto tile_of = [&](int lin, int& tile, int& g) {
-    const int lead = p.lead_tiles < p.n_tiles ? p.lead_tiles : p.n_tiles;
-    if (lin < lead * p.BH) {
-      tile = lin / p.BH;
-      g = lin % p.BH;
+  // A lead tile counts `splits` work items (consecutive), each a share of
+  // its key blocks.  The split count is chosen here, the same in every CTA
+  // (from the CSR's live-block total): a lead tile (about nbk blocks) is cut
+  // so that no share exceeds the average work of a CTA, up to the host's cap.
+  const int lead = p.lead_tiles < p.n_tiles ? p.lead_tiles : p.n_tiles;
+  __shared__ int s_splits;
+  if (warp == 0) {
+    int sp = 1;
+    if (p.splits > 1 && lead > 0) {
+      long long nnz = 0;
+      for (int gg = lane; gg < p.BH; gg += 32) {
+        const int32_t* rp = p.row_ptr + static_cast<int64_t>(gg) * (p.nbq + 1);
+        nnz += static_cast<long long>(max(0, rp[p.nbq] - rp[0]));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) nnz += __shfl_xor_sync(0xffffffffu, nnz, off);
+      const long long work = nnz * p.bm / kBM;  // blocks of 128-row tiles
+      const long long want = work > 0 ? (static_cast<long long>(p.nbk) * gridDim.x + work - 1) / work : 1;
+      sp = static_cast<int>(want < p.splits ? (want < 1 ? 1 : want) : p.splits);
+    }
+    if (lane == 0) s_splits = sp;
+  }
+  __syncthreads();
+  const int n_split = s_splits;
+  const int n_total = (lead * n_split + p.n_tiles - lead) * p.BH;
+  auto tile_of = [&](int lin, int& tile, int& g, int& split) {
+    if (lin < lead * p.BH * n_split) {
+      split = lin % n_split;
+      const int t2 = lin / n_split;
+      tile = t2 / p.BH;
+      g = t2 % p.BH;
     } else {
-      const int rest = p.n_tiles - lead, l2 = lin - lead * p.BH;
+      const int rest = p.n_tiles - lead, l2 = lin - lead * p.BH * n_split;
       g = l2 / rest;
       tile = lead + l2 % rest;
+      split = 0;
     }
   };
+  const bool split_on = n_split > 1;
 
   const uint32_t sQ = smem_u32(smem + L::kOffQ);
   const uint32_t sK0 = smem_u32(smem + L::kOffK);
@@ -352,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   volatile int* tile_slot = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);  // [2]
   volatile int* tile_cnt = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 16);  // [2] list lengths
+  volatile int* tile_off = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 24);  // [2] first list entry
   uint16_t* list_base = reinterpret_cast<uint16_t*>(smem + L::kOffList);            // [2][list_cap]
   uint32_t* list_bits = reinterpret_cast<uint32_t*>(smem + L::kOffList + 4 * p.list_cap);
   float* pool_lse = reinterpret_cast<float*>(list_bits + 2 * ((p.nbk + 31) / 32));  // [2][128]
@@ -421,17 +458,23 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int slot = ti & 1;
       ok = mbar_wait(bar_tile_empty(slot), ((ti >> 1) & 1) ^ 1, abort_flag, p.status, p.budget_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
-      int tile = 0, g = 0, n_blk = 0;
+      int tile = 0, g = 0, split = 0, n_blk = 0, off = 0;
       uint16_t* lst = list_base + slot * p.list_cap;
       if (lin < n_total) {
-        tile_of(lin, tile, g);
+        tile_of(lin, tile, g, split);
         n_blk = build_tile_list(p, g, tile, lst, list_bits, lane);
+        if (split_on && tile < lead) {  // this item's share of the lead tile's blocks
+          off = n_blk * split / n_split;
+          n_blk = n_blk * (split + 1) / n_split - off;
+        }
       }
+      lst += off;
       __threadfence_block();
       __syncwarp();
       if (lane == 0) {
         tile_slot[slot] = lin;
         tile_cnt[slot] = n_blk;
+        tile_off[slot] = off;
         mbar_arrive(bar_tile_full(slot));
       }
       __syncwarp();
@@ -659,8 +702,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive(bar_tile_empty(slot));
         break;
       }
-      int tile, g;
-      tile_of(lin, tile, g);
+      int tile, g, split;
+      tile_of(lin, tile, g, split);
       if (!__all_sync(0xffffffffu, mbar_wait(bar_pool_full(slot), par, abort_flag, p.status, p.budget_ns))) break;
       const float lse0 = pool_lse[slot * kBM + t], lse1 = pool_lse[slot * kBM + t + 64];
       const float* scr = p.pool_scratch + (static_cast<int64_t>(blockIdx.x) * 2 + slot) * p.list_cap * kBM;
@@ -740,8 +783,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(bar_tile_empty(slot));
       break;
     }
-    int tile, g;
-    tile_of(lin, tile, g);
+    int tile, g, split;
+    tile_of(lin, tile, g, split);
+    const bool split_item = split_on && tile < lead;
     const int b = g / p.H, h = g % p.H;
     const int q0 = tile * kBM;
     float m_run = -INFINITY, l_run = 0.f;
@@ -765,7 +809,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         fbits = __ldg(p.frame_bits + static_cast<int64_t>(g) * p.frames + fq);
       }
     }
-    const uint16_t* lst = list_base + slot * p.list_cap;
+    const uint16_t* lst = list_base + slot * p.list_cap + tile_off[slot];
     if constexpr (kPool) {
       // this parity's scratch slot is free once the reducer pooled the tile
       // two tiles back
@@ -992,6 +1036,77 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
                    2 * (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
                         static_cast<int64_t>(qrow) * p.o_ss);
+    auto store_row = [&](const float* vals, float scale) {
+#pragma unroll
+      for (int v = 0; v < kD / 8; ++v) {
+        uint4 w;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = vals[v * 8 + 2 * e] * scale, hi = vals[v * 8 + 2 * e + 1] * scale;
+          pw[e] = kBF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+        }
+        reinterpret_cast<uint4*>(dst)[v] = w;
+      }
+    };
+    if (split_item) {
+      // a share of a lead tile: the row's unnormalised O, m and l go to the
+      // split buffer; the last share of the row to finish merges them all
+      float* part = p.split_part +
+                    ((((static_cast<int64_t>(g) * lead + tile) * n_split + split) * kBM) + row) * kSplitRow;
+#pragma unroll
+      for (int c = 0; c < kD / 32; ++c) {
+        uint32_t orr[32];
+        if (have_o) {
+          tmem_ld32(tO + 32 * c, orr);
+          tmem_wait_ld(orr);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) orr[e] = 0u;
+        }
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          reinterpret_cast<float4*>(part)[c * 8 + v] =
+              make_float4(__uint_as_float(orr[4 * v]), __uint_as_float(orr[4 * v + 1]),
+                          __uint_as_float(orr[4 * v + 2]), __uint_as_float(orr[4 * v + 3]));
+      }
+      part[kD] = m_run;
+      part[kD + 1] = (have_o || j == 0) ? l_run : 0.f;
+      __threadfence();
+      int* cnt = p.split_cnt + (static_cast<int64_t>(g) * lead + tile) * kBM + row;
+      if (atomicAdd(cnt, 1) == n_split - 1) {
+        __threadfence();
+        const float* base = p.split_part + (((static_cast<int64_t>(g) * lead + tile) * n_split) * kBM + row) * kSplitRow;
+        const int64_t sstride = static_cast<int64_t>(kBM) * kSplitRow;
+        float mm = -INFINITY;
+        for (int sp = 0; sp < n_split; ++sp) {
+          const float ls = __ldcg(base + sp * sstride + kD + 1);
+          if (ls > 0.f) mm = fmaxf(mm, __ldcg(base + sp * sstride + kD));
+        }
+        float acc[kD];
+#pragma unroll
+        for (int d = 0; d < kD; ++d) acc[d] = 0.f;
+        float ll = 0.f;
+        for (int sp = 0; sp < n_split; ++sp) {
+          const float* ps = base + sp * sstride;
+          const float ls = __ldcg(ps + kD + 1);
+          if (!(ls > 0.f)) continue;
+          const float wgt = ex2_approx(__ldcg(ps + kD) - mm);
+          ll += ls * wgt;
+#pragma unroll
+          for (int d4 = 0; d4 < kD / 4; ++d4) {
+            const float4 o4 = __ldcg(reinterpret_cast<const float4*>(ps) + d4);
+            acc[4 * d4] += o4.x * wgt;
+            acc[4 * d4 + 1] += o4.y * wgt;
+            acc[4 * d4 + 2] += o4.z * wgt;
+            acc[4 * d4 + 3] += o4.w * wgt;
+          }
+        }
+        *cnt = 0;
+        // no visible key in any share: 0 / 0 = NaN, as the unsplit path
+        if (ok && !*abort_flag && qrow < p.Sq) store_row(acc, 1.f / ll);
+      }
+    } else {
     const bool write = (j == 0 || have_o) && ok && !*abort_flag && qrow < p.Sq;
 #pragma unroll
     for (int c = 0; c < kD / 32; ++c) {
@@ -1017,6 +1132,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           reinterpret_cast<uint4*>(dst)[c * 4 + v] = w;
         }
       }
+    }
     }
     // the tile's block list is no longer read: the producer may refill the slot
     mbar_arrive(bar_tile_empty(slot));
@@ -1058,6 +1174,34 @@ int32_t tile_counter_slot(unsigned int** out) {
   return SAF_OK;
 }
 
+// Split buffers of the lead tiles (static per device, like the tile
+// counters): partial rows [heads x lead tiles x splits x 128 x 66] fp32 and
+// one counter per (head, lead tile, row).  A launch whose split buffers would
+// not fit runs its lead tiles unsplit.
+constexpr int64_t kSplitFloats = int64_t(4) << 20;  // 16 MiB
+constexpr int64_t kSplitCnts = int64_t(1) << 18;    // 1 MiB
+__device__ __align__(16) float g_split_part[kSplitFloats];
+__device__ int g_split_cnt[kSplitCnts];
+float* g_split_part_base[kMaxDevices] = {};
+int* g_split_cnt_base[kMaxDevices] = {};
+
+int32_t split_buffers(float** part, int** cnt) {
+  int dev = 0;
+  SAF_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return SAF_ERR_UNSUPPORTED;
+  if (g_split_part_base[dev] == nullptr) {
+    void* a = nullptr;
+    void* c = nullptr;
+    SAF_CUDA_TRY(cudaGetSymbolAddress(&a, g_split_part));
+    SAF_CUDA_TRY(cudaGetSymbolAddress(&c, g_split_cnt));
+    g_split_cnt_base[dev] = static_cast<int*>(c);
+    g_split_part_base[dev] = static_cast<float*>(a);
+  }
+  *part = g_split_part_base[dev];
+  *cnt = g_split_cnt_base[dev];
+  return SAF_OK;
+}
+
 template <int BN, bool kBias, bool kBF16, int kMask>
 int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                        BsaParams p, int n_tiles, cudaStream_t stream) {
@@ -1080,7 +1224,23 @@ int32_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
   if (rc != SAF_OK) return rc;
   p.n_tiles = n_tiles;
   p.BH = p.B * p.H;
-  const int64_t total = static_cast<int64_t>(n_tiles) * p.BH;
+  // Lead tiles (dense text rows: every key block) are the longest work items;
+  // with few heads per GPU a single one outlasts the rest of the launch, so
+  // their key blocks may be split over several items.  The host sets the cap
+  // (buffer capacity, at most 8); the kernel picks the count from the CSR.
+  // The grid is sized for the cap; CTAs without an item return at once.
+  const int lead = p.lead_tiles < n_tiles ? p.lead_tiles : n_tiles;
+  p.splits = 1;
+  if (lead > 0 && kMask != kMaskPool && kMask != kMaskKeys) {
+    const int64_t items = static_cast<int64_t>(lead) * p.BH;
+    int sp = static_cast<int>(std::min<int64_t>(8, (2 * sms + items - 1) / items));
+    if (sp > 1 && items * sp * kBM * kSplitRow <= kSplitFloats && items * kBM <= kSplitCnts) {
+      if ((rc = split_buffers(&p.split_part, &p.split_cnt)) != SAF_OK) return rc;
+      SAF_CUDA_TRY(cudaMemsetAsync(p.split_cnt, 0, static_cast<size_t>(items * kBM) * sizeof(int), stream));
+      p.splits = sp;
+    }
+  }
+  const int64_t total = (static_cast<int64_t>(lead) * p.splits + n_tiles - lead) * p.BH;
   const int grid = static_cast<int>(total < 2 * sms ? total : 2 * sms);  // two CTAs per SM
   kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
   SAF_CUDA_TRY(cudaGetLastError());

@@ -197,8 +197,11 @@ def test_rejects_cpu_tensors():
 
 @pytest.mark.parametrize("bm", [128, 64])
 def test_lead_rows_schedule_does_not_change_results(cuda_device, bm):
-    """The dense-row scheduling hint only reorders CTAs: outputs are bitwise
-    identical for any value."""
+    """The dense-row hint reorders the work and, with few heads per GPU,
+    splits the lead tiles' key blocks over several work items merged per row
+    (fp32 partials): outputs stay within the oracle's tolerance and within
+    one output rounding of the unsplit launch; the rows outside the lead
+    tiles are bitwise identical."""
     B, H, S, D = 2, 3, 1500, 64
     q, k, v = (t.to(cuda_device) for t in _inputs(B, H, S, S, D, torch.bfloat16, seed=41))
     nb = math.ceil(S / bm)
@@ -209,4 +212,11 @@ def test_lead_rows_schedule_does_not_change_results(cuda_device, bm):
         csr = kernels.mask_to_csr(mask, bm, bm, dense_rows=lead)
         outs.append(kernels.bsa_fwd(q, k, v, csr, 0.125))
     torch.cuda.synchronize()
-    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    ref = oatt.block_sparse_attention(q.cpu(), k.cpu(), v.cpu(), mask.cpu().numpy(), 0.125, bm, bm)
+    for o in outs:
+        _compare(o, ref, 2e-2)
+    # lead = 3 mask rows: the split covers the first ceil(3 * bm / 128) tiles
+    split_rows = math.ceil(3 * bm / 128) * 128
+    assert torch.equal(outs[0][:, :, split_rows:], outs[1][:, :, split_rows:])
+    for o in outs[1:]:
+        assert float((o.float() - outs[0].float()).abs().max()) <= 2e-2

@@ -239,25 +239,34 @@ def test_probe_update_gap(full_run, cuda_device):
 
 def test_probe_score_mode_follows_the_cumulative_rule(cuda_device):
     """probe_solver(type="score") (:64-84): per batch, the keys by descending
-    mass up to the first cumulative share >= percentile -- on the probe
-    kernel's mass, checked against the oracle's mass and the same rule."""
+    mass up to the first cumulative share >= percentile.  The rule is checked
+    exactly on the probe kernel's own mass (the cumulative sum is a 16-bit
+    scan, whose rounding differs between a CPU and a GPU), and that mass
+    against the oracle's."""
     g = torch.Generator().manual_seed(41)
     q = (torch.randn(2, 2, 300, 64, generator=g) * 1.2).to(torch.bfloat16)
     k = torch.randn(2, 2, 700, 64, generator=g).to(torch.bfloat16)
     solver = lga.probe_solver(percentile=0.3, sample_num=64, type="score")
+    qd, kd = q.to(cuda_device), k.to(cuda_device)
     torch.cuda.manual_seed(7)
-    got = solver._probe(q.to(cuda_device), k.to(cuda_device))
+    got = solver._probe(qd, kd)
+    torch.cuda.manual_seed(7)
+    mass = solver._mass(qd, kd)
     torch.cuda.manual_seed(7)
     samples = torch.randint(0, 300, (2, 1, 64), device=cuda_device).view(2, -1).cpu().numpy()
-    mass = olg.probe_mass(q, k, samples, row_offset=0)
+    ref = olg.probe_mass(q, k, samples, row_offset=0)
+    diff = mass.cpu().numpy() != ref
+    assert diff.sum() <= 4, diff.sum()
+    assert np.all(np.abs(mass.cpu().numpy() - ref)[diff] <= np.abs(ref[diff]) * 2.0 ** -7)
     for b in range(2):
-        v = torch.from_numpy(mass[b]).to(torch.bfloat16)
-        vals, idx = torch.sort(v, descending=True)
+        vals, idx = torch.sort(mass[b].to(torch.bfloat16), descending=True)
         cum = (vals / (2 * 64)).cumsum(dim=-1)
         n = int(torch.searchsorted(cum, 0.3)) + 1
-        sel = got[b].cpu().numpy()
-        assert abs(sel.size - n) <= 1
-        # every selected key has a mass at or above the oracle's (n + 1)-th
-        # largest (ties may be broken either way)
-        assert float(v[torch.from_numpy(sel.astype(np.int64))].float().min()) >= float(vals[min(n, vals.numel() - 1)])
-
+        assert n < vals.numel()
+        sel = got[b]
+        assert sel.numel() == n
+        # the first n by descending mass (a tie at the cut may go either way)
+        assert float(vals[n - 1]) >= float(vals[n])
+        picked = mass[b].to(torch.bfloat16)[sel].float()
+        assert float(picked.min()) >= float(vals[n - 1])
+        assert torch.unique(sel).numel() == n

@@ -552,100 +552,98 @@ template <typename T, bool kShort>
 __global__ void __launch_bounds__(256, kShort ? 4 : 3) tome_exact_kernel(const ExactParams e) {
   const int lane = threadIdx.x & 31;
   constexpr bool short_rows = kShort;  // Cp <= 32 * kExactCols
-  {
-    const int b = blockIdx.y;
-    const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (i >= e.Ns) return;
-    const int64_t ri = static_cast<int64_t>(b) * e.Ns + i;
-    const T* a = static_cast<const T*>(e.A) + ri * e.Cp;
-    // independent loads first
-    const double na = e.na[ri];
-    const float cvl = lane < kCand ? e.cand_val[ri * kCand + lane] : -INFINITY;
-    const int cil = lane < kCand ? e.cand_idx[ri * kCand + lane] : -1;
-    T av[kExactCols];  // 16-bit values; a zero pad adds +0 and changes no sum
+  const int b = blockIdx.y;
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (i >= e.Ns) return;
+  const int64_t ri = static_cast<int64_t>(b) * e.Ns + i;
+  const T* a = static_cast<const T*>(e.A) + ri * e.Cp;
+  // independent loads first
+  const double na = e.na[ri];
+  const float cvl = lane < kCand ? e.cand_val[ri * kCand + lane] : -INFINITY;
+  const int cil = lane < kCand ? e.cand_idx[ri * kCand + lane] : -1;
+  T av[kExactCols];  // 16-bit values; a zero pad adds +0 and changes no sum
 #pragma unroll
-    for (int i = 0; i < kExactCols; ++i) {
-      const int c = lane + 32 * i;
-      av[i] = (short_rows && c < e.Cp) ? a[c] : T(0.f);
+  for (int q = 0; q < kExactCols; ++q) {
+    const int c = lane + 32 * q;
+    av[q] = (short_rows && c < e.Cp) ? a[c] : T(0.f);
+  }
+  const double sa = __dsqrt_rn(na);
+  const double tau = 2.0 * kEps * sa;  // in units of s~ = dot * (1/|b|)
+  const float cv0 = __shfl_sync(0xffffffffu, cvl, 0);
+  // The score kernel kept every column within tau of the row's maximum
+  // unless it marked the row incomplete (index -2 in the last slot).
+  const bool complete = e.Nd <= kCand || __shfl_sync(0xffffffffu, cil, kCand - 1) != -2;
+  // A candidate can be the exact best only if its tensor-core score is
+  // within tau of the top one (each score is within tau / 2 of its exact
+  // value).
+  const float keep_above = static_cast<float>(static_cast<double>(cv0) - tau * (1.0 + 1.0 / 256.0));
+  double best = -INFINITY;
+  int bj = 0x7fffffff;
+  auto take = [&](double d, int j) {
+    const double cs = __ddiv_rn(d, __dmul_rn(sa, __dsqrt_rn(e.nb[static_cast<int64_t>(b) * e.Nd + j])));
+    if (cs > best || (cs == best && j < bj)) {
+      best = cs;
+      bj = j;
     }
-    const double sa = __dsqrt_rn(na);
-    const double tau = 2.0 * kEps * sa;  // in units of s~ = dot * (1/|b|)
-    const float cv0 = __shfl_sync(0xffffffffu, cvl, 0);
-    // The score kernel kept every column within tau of the row's maximum
-    // unless it marked the row incomplete (index -2 in the last slot).
-    const bool complete = e.Nd <= kCand || __shfl_sync(0xffffffffu, cil, kCand - 1) != -2;
-    // A candidate can be the exact best only if its tensor-core score is
-    // within tau of the top one (each score is within tau / 2 of its exact
-    // value).
-    const float keep_above = static_cast<float>(static_cast<double>(cv0) - tau * (1.0 + 1.0 / 256.0));
-    double best = -INFINITY;
-    int bj = 0x7fffffff;
-    auto take = [&](double d, int j) {
-      const double cs = __ddiv_rn(d, __dmul_rn(sa, __dsqrt_rn(e.nb[static_cast<int64_t>(b) * e.Nd + j])));
-      if (cs > best || (cs == best && j < bj)) {
-        best = cs;
-        bj = j;
-      }
-    };
-    const T* bbase = static_cast<const T*>(e.Bm) + static_cast<int64_t>(b) * e.Nd * e.Cp;
-    if constexpr (kShort) {
-      if (!complete) {  // every dst, four at a time
+  };
+  const T* bbase = static_cast<const T*>(e.Bm) + static_cast<int64_t>(b) * e.Nd * e.Cp;
+  if constexpr (kShort) {
+    if (!complete) {  // every dst, four at a time
 #pragma unroll 1
-        for (int j0 = 0; j0 < e.Nd; j0 += 4) {
-          T bv[4][kExactCols];
+      for (int j0 = 0; j0 < e.Nd; j0 += 4) {
+        T bv[4][kExactCols];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const T* bj_row = bbase + static_cast<int64_t>(min(j0 + u, e.Nd - 1)) * e.Cp;
+        for (int u = 0; u < 4; ++u) {
+          const T* bj_row = bbase + static_cast<int64_t>(min(j0 + u, e.Nd - 1)) * e.Cp;
 #pragma unroll
-            for (int q = 0; q < kExactCols; ++q) {
-              const int c = lane + 32 * q;
-              bv[u][q] = c < e.Cp ? bj_row[c] : T(0.f);
-            }
+          for (int q = 0; q < kExactCols; ++q) {
+            const int c = lane + 32 * q;
+            bv[u][q] = c < e.Cp ? bj_row[c] : T(0.f);
           }
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (j0 + u < e.Nd) take(held_dot<T>(av, bv[u]), j0 + u);
         }
-      } else {
-      uint32_t m = __ballot_sync(0xffffffffu, lane < kCand && lane < e.Nd && cil >= 0 &&
-                                                  (lane == 0 || cvl >= keep_above));
-      while (m != 0u) {
-        const int k0 = __ffs(m) - 1;
-        m &= m - 1u;
-        const int k1 = m != 0u ? __ffs(m) - 1 : k0;
-        if (m != 0u) m &= m - 1u;
-        const int j0 = __shfl_sync(0xffffffffu, cil, k0), j1 = __shfl_sync(0xffffffffu, cil, k1);
-        const T* b0 = bbase + static_cast<int64_t>(j0) * e.Cp;
-        const T* b1 = bbase + static_cast<int64_t>(j1) * e.Cp;
-        T bv0[kExactCols], bv1[kExactCols];
 #pragma unroll
-        for (int i = 0; i < kExactCols; ++i) {
-          const int c = lane + 32 * i;
-          bv0[i] = c < e.Cp ? b0[c] : T(0.f);
-          bv1[i] = (k1 != k0 && c < e.Cp) ? b1[c] : T(0.f);
-        }
-        take(held_dot<T>(av, bv0), j0);
-        if (k1 != k0) take(held_dot<T>(av, bv1), j1);
-      }
+        for (int u = 0; u < 4; ++u)
+          if (j0 + u < e.Nd) take(held_dot<T>(av, bv[u]), j0 + u);
       }
     } else {
-      auto consider = [&](int j) { take(exact_dot(a, bbase + static_cast<int64_t>(j) * e.Cp, e.Cp, lane), j); };
-      if (complete) {
-#pragma unroll 1
-        for (int k = 0; k < kCand && k < e.Nd; ++k) {
-          const int j = __shfl_sync(0xffffffffu, cil, k);
-          const float cvk = __shfl_sync(0xffffffffu, cvl, k);
-          if (j >= 0 && (k == 0 || cvk >= keep_above)) consider(j);
-        }
-      } else {
-#pragma unroll 1
-        for (int j = 0; j < e.Nd; ++j) consider(j);
+    uint32_t m = __ballot_sync(0xffffffffu, lane < kCand && lane < e.Nd && cil >= 0 &&
+                                                (lane == 0 || cvl >= keep_above));
+    while (m != 0u) {
+      const int k0 = __ffs(m) - 1;
+      m &= m - 1u;
+      const int k1 = m != 0u ? __ffs(m) - 1 : k0;
+      if (m != 0u) m &= m - 1u;
+      const int j0 = __shfl_sync(0xffffffffu, cil, k0), j1 = __shfl_sync(0xffffffffu, cil, k1);
+      const T* b0 = bbase + static_cast<int64_t>(j0) * e.Cp;
+      const T* b1 = bbase + static_cast<int64_t>(j1) * e.Cp;
+      T bv0[kExactCols], bv1[kExactCols];
+#pragma unroll
+      for (int q = 0; q < kExactCols; ++q) {
+        const int c = lane + 32 * q;
+        bv0[q] = c < e.Cp ? b0[c] : T(0.f);
+        bv1[q] = (k1 != k0 && c < e.Cp) ? b1[c] : T(0.f);
       }
+      take(held_dot<T>(av, bv0), j0);
+      if (k1 != k0) take(held_dot<T>(av, bv1), j1);
     }
-    if (lane == 0) {
-      e.node_max[ri] = best;
-      e.node_idx[ri] = bj;
     }
+  } else {
+    auto consider = [&](int j) { take(exact_dot(a, bbase + static_cast<int64_t>(j) * e.Cp, e.Cp, lane), j); };
+    if (complete) {
+#pragma unroll 1
+      for (int k = 0; k < kCand && k < e.Nd; ++k) {
+        const int j = __shfl_sync(0xffffffffu, cil, k);
+        const float cvk = __shfl_sync(0xffffffffu, cvl, k);
+        if (j >= 0 && (k == 0 || cvk >= keep_above)) consider(j);
+      }
+    } else {
+#pragma unroll 1
+      for (int j = 0; j < e.Nd; ++j) consider(j);
+    }
+  }
+  if (lane == 0) {
+    e.node_max[ri] = best;
+    e.node_idx[ri] = bj;
   }
 }
 

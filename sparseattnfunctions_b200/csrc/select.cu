@@ -163,18 +163,18 @@ __device__ __forceinline__ bool better(double a, int ia, double b, int ib) {
   return a > b || (a == b && ia < ib);
 }
 
-// grid (B*H, ceil(nbq / 16)), 256 threads; each warp owns kRowsPerWarp
+// grid (B*H, ceil(nbq / (8 RPW))), 256 threads; each warp owns RPW
 // consecutive row blocks, so every key mean staged in shared memory (32 dims
-// at a time) serves two rows (two rather than four: twice the CTAs, and the
-// serial top-k rounds of a warp cover half the rows).  Every lane owns columns lane + 32m (m < M)
-// and accumulates their fp64 scores with d ascending (separate multiply and
-// add, no contraction).  The top-k is k rounds of a warp arg-max (ties ->
-// lower column).
-constexpr int kRowsPerWarp = 2;
-constexpr int kRowsPerCta = 8 * kRowsPerWarp;
-
-template <int M>
+// at a time) serves RPW rows: two when the grid fills the GPU (the staged
+// means serve twice the rows), one when few heads share a GPU (twice the
+// CTAs, and the serial top-k rounds of a warp cover half the rows).  Every
+// lane owns columns lane + 32m (m < M) and accumulates their fp64 scores
+// with d ascending (separate multiply and add, no contraction).  The top-k
+// is k rounds of a warp arg-max (ties -> lower column).
+template <int M, int RPW>
 __global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
+  constexpr int kRowsPerWarp = RPW;
+  constexpr int kRowsPerCta = 8 * RPW;
   extern __shared__ double ks[];  // [nbk][kDChunk+1] then [32][kDChunk+1]
   double* qs = ks + a.nbk * (kDChunk + 1);
   const int g = blockIdx.x;
@@ -476,14 +476,27 @@ int32_t pool_dispatch(const saf_tensor4* q, const saf_tensor4* k, int bm, int bn
   }
 }
 
-template <int M>
-int32_t launch_score(const SelectArgs& a, int64_t BH, cudaStream_t st) {
+template <int M, int RPW>
+int32_t launch_score_rpw(const SelectArgs& a, int64_t BH, cudaStream_t st) {
+  constexpr int kRowsPerCta = 8 * RPW;
   const size_t smem = (static_cast<size_t>(a.nbk) + kRowsPerCta) * (kDChunk + 1) * sizeof(double);
-  SAF_CUDA_TRY(cudaFuncSetAttribute(score_topk_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  SAF_CUDA_TRY(cudaFuncSetAttribute(score_topk_kernel<M, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
   dim3 grid(static_cast<unsigned>(BH), (a.nbq + kRowsPerCta - 1) / kRowsPerCta);
-  score_topk_kernel<M><<<grid, 256, smem, st>>>(a);
+  score_topk_kernel<M, RPW><<<grid, 256, smem, st>>>(a);
   return SAF_OK;
+}
+
+// Two rows a warp unless that grid leaves SMs without a CTA (measured at
+// CogVideoX-2B shape: 8 heads 37.0 -> 32.9 us with one row a warp, 30 heads
+// 68.7 -> 72.3 us, so the switch sits at one CTA per SM).
+template <int M>
+int32_t launch_score(const SelectArgs& a, int64_t BH, cudaStream_t st) {
+  int dev = 0, sms = 0;
+  SAF_CUDA_TRY(cudaGetDevice(&dev));
+  SAF_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t ctas2 = BH * ((a.nbq + 15) / 16);
+  return ctas2 >= sms ? launch_score_rpw<M, 2>(a, BH, st) : launch_score_rpw<M, 1>(a, BH, st);
 }
 
 }  // namespace

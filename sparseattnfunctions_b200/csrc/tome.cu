@@ -72,8 +72,9 @@ struct ScoreLayoutT {
   static constexpr int kOffRing = kRes ? kResChunks * kABytes : 0;
   static constexpr int kOffCand = kOffRing + kStages * kStageBytes;  // [2][128][8] (val, idx)
   static constexpr int kOffBar = kOffCand + 2 * kTM * kCand * 8;
-  // full[S], empty[S], acc_full[2], acc_empty[2], drain, xend, a_full
-  static constexpr int kNumBars = 2 * kStages + 7;
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain, xend, a_full,
+  // a_empty, xread
+  static constexpr int kNumBars = 2 * kStages + 9;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kDynSmem = kOffMisc + 16 + 1024;
 };
@@ -110,7 +111,11 @@ __device__ __forceinline__ float pick32(const float (&sc)[32], int e) {
   return (e & 16) ? l4[1] : l4[0];
 }
 
-// grid (ceil(Ns/128), B).  One CTA per SM (TMEM: two 256-column accumulators).
+// Persistent: one CTA per SM (TMEM: two 256-column accumulators) takes the
+// work items (128 src rows of one batch row, batch-row-major) i = blockIdx.x,
+// blockIdx.x + gridDim.x, ...; the B ring, the accumulators and the resident
+// A carry over from item to item, so an item's first products are made while
+// the epilogue still works on the previous item's last tiles.
 template <bool kBF16, bool kRes>
 __global__ void __launch_bounds__(kScoreThreads, 1)
     tome_score_kernel(const __grid_constant__ CUtensorMap tm_a,
@@ -120,7 +125,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTM, b = blockIdx.y;
+  const int mblocks = (p.Ns + kTM - 1) / kTM, n_items = mblocks * p.B;
   const int n_tiles = (p.Nd + kTN - 1) / kTN, k_chunks = p.Cp / kTK;
   const uint32_t ring = smem_u32(smem + L::kOffRing);
   const uint32_t bar0 = smem_u32(smem + L::kOffBar);
@@ -130,7 +135,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   auto bar_acc_empty = [&](int i) { return bar0 + 8u * (2 * kStages + 2 + i); };
   const uint32_t bar_drain = bar0 + 8u * (2 * kStages + 4);
   const uint32_t bar_xend = bar0 + 8u * (2 * kStages + 5);
-  const uint32_t bar_a = bar0 + 8u * (2 * kStages + 6);  // resident A landed (kRes)
+  const uint32_t bar_a = bar0 + 8u * (2 * kStages + 6);        // resident A landed (kRes)
+  const uint32_t bar_a_empty = bar0 + 8u * (2 * kStages + 7);  // its products are done (kRes)
+  const uint32_t bar_xread = bar0 + 8u * (2 * kStages + 8);    // the half-merge slots were read
   const uint32_t sA = smem_u32(smem + L::kOffA);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
@@ -147,6 +154,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     mbar_init(bar_drain, 1);
     mbar_init(bar_xend, 256);
     mbar_init(bar_a, 1);
+    mbar_init(bar_a_empty, 1);
+    mbar_init(bar_xread, 128);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_a);
@@ -163,11 +172,16 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    int issued = 0;
+    int issued = 0, items = 0, a_loads = 0;
     if (lane == 0) {
+      for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++items) {
+      const int m0 = (item % mblocks) * kTM, b = item / mblocks;
       if constexpr (kRes) {
+        // the previous item's products must be done with the resident A
+        if (items > 0 && !mbar_wait(bar_a_empty, (items - 1) & 1, abort_flag, p.status, p.budget_ns)) break;
         mbar_arrive_expect_tx(bar_a, k_chunks * L::kABytes);
         for (int kc = 0; kc < k_chunks; ++kc) tma_load_3d(sA + kc * L::kABytes, &tm_a, bar_a, kc * kTK, m0, b);
+        ++a_loads;
       }
       for (int nt = 0; nt < n_tiles; ++nt) {
         for (int kc = 0; kc < k_chunks; ++kc, ++issued) {
@@ -185,8 +199,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         }
         if (*abort_flag) break;
       }
+      }
       // drain: wait for the last load of every stage (and the resident A)
-      if constexpr (kRes) mbar_drain(bar_a, 0, p.status);
+      if constexpr (kRes) {
+        if (a_loads > 0) mbar_drain(bar_a, (a_loads - 1) & 1, p.status);
+      }
       for (int s = 0; s < kStages && s < issued; ++s) {
         const int last = s + ((issued - 1 - s) / kStages) * kStages;
         mbar_drain(bar_full(s), (last / kStages) & 1, p.status);
@@ -197,12 +214,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdesc = idesc_f16(kTM, kTN, kBF16, false, false);
-      int used = 0;
+      int used = 0, ntg = 0;  // K chunks consumed, tiles made (all items)
       bool ok = true;
-      if constexpr (kRes) ok = mbar_wait(bar_a, 0, abort_flag, p.status, p.budget_ns);
-      for (int nt = 0; nt < n_tiles && ok; ++nt) {
-        const int buf = nt & 1;
-        if (!mbar_wait(bar_acc_empty(buf), ((nt >> 1) & 1) ^ 1, abort_flag, p.status,
+      for (int item = blockIdx.x, items = 0; item < n_items && ok; item += gridDim.x, ++items) {
+      if constexpr (kRes) ok = mbar_wait(bar_a, items & 1, abort_flag, p.status, p.budget_ns);
+      for (int nt = 0; nt < n_tiles && ok; ++nt, ++ntg) {
+        const int buf = ntg & 1;
+        if (!mbar_wait(bar_acc_empty(buf), ((ntg >> 1) & 1) ^ 1, abort_flag, p.status,
                        p.budget_ns)) {
           ok = false;
           break;
@@ -229,6 +247,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         }
         if (ok) tc_commit(bar_acc_full(buf));
       }
+      // the resident A is free once this item's products are done
+      if constexpr (kRes) {
+        if (ok) tc_commit(bar_a_empty);
+      }
+      }
       tc_commit(bar_drain);
       mbar_drain(bar_drain, 0, p.status);
     }
@@ -238,6 +261,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const int quarter = warp & 3, chalf = (warp - 4) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    bool ok = true;
+    int ntg = 0;  // tiles taken (all items)
+    for (int item = blockIdx.x, items = 0; item < n_items && ok; item += gridDim.x, ++items) {
+    const int m0 = (item % mblocks) * kTM, b = item / mblocks;
     const float* rinv = p.rinv_b + static_cast<int64_t>(b) * ((p.Nd + 3) & ~3);
     // Candidates of this thread's half of the row: every column whose score
     // came within tau of the running maximum when it was seen (the only
@@ -261,15 +288,14 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       if (ci[kCand - 1] >= 0 && fminf(sv, cv[kCand - 1]) >= thr) ovf = true;
       cand_insert(cv, ci, sv, j);
     };
-    bool ok = true;
     float4 rv_next[8];
     if (chalf * (kTN / 2) + 32 <= p.Nd) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) rv_next[i] = __ldg(reinterpret_cast<const float4*>(rinv + chalf * (kTN / 2)) + i);
     }
-    for (int nt = 0; nt < n_tiles; ++nt) {
-      const int buf = nt & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_acc_full(buf), (nt >> 1) & 1, abort_flag,
+    for (int nt = 0; nt < n_tiles; ++nt, ++ntg) {
+      const int buf = ntg & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_acc_full(buf), (ntg >> 1) & 1, abort_flag,
                                               p.status, p.budget_ns))) {
         ok = false;
         break;
@@ -366,14 +392,21 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     // merge the two column halves of every row
     float2* cand = reinterpret_cast<float2*>(smem + L::kOffCand);
     if (chalf == 1) {
+      // the slots are free once the other half has read the previous item's
+      if (ok && items > 0 &&
+          !__all_sync(0xffffffffu, mbar_wait(bar_xread, (items - 1) & 1, abort_flag, p.status, p.budget_ns)))
+        ok = false;
+      if (ok) {
 #pragma unroll
-      for (int i = 0; i < kCand; ++i)
-        cand[(kTM + row) * kCand + i] = make_float2(cv[i], __int_as_float(ci[i]));
-      cand[row * kCand] = make_float2(run_max, __int_as_float(ovf ? 1 : 0));
+        for (int i = 0; i < kCand; ++i)
+          cand[(kTM + row) * kCand + i] = make_float2(cv[i], __int_as_float(ci[i]));
+        cand[row * kCand] = make_float2(run_max, __int_as_float(ovf ? 1 : 0));
+      }
     }
     mbar_arrive(bar_xend);
-    const bool have = ok && __all_sync(0xffffffffu, mbar_wait(bar_xend, 0, abort_flag, p.status,
+    const bool have = ok && __all_sync(0xffffffffu, mbar_wait(bar_xend, items & 1, abort_flag, p.status,
                                                                p.budget_ns));
+    if (!have) ok = false;
     if (have && chalf == 0 && m0 + row < p.Ns && !*abort_flag) {
       const float2 hdr = cand[row * kCand];
       run_max = fmaxf(run_max, hdr.x);
@@ -393,6 +426,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         p.cand_val[base + i] = cv[i];
       }
     }
+    if (chalf == 0) mbar_arrive(bar_xread);
+    }  // items
   }
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
@@ -1110,7 +1145,12 @@ extern "C" int32_t saf_tome_match(const void* metric, int32_t dtype, int64_t B, 
   if ((rc = make_rows_map(&mb, Bm, B, Nd, Cp, kTN, bf16)) != SAF_OK) return rc;
   ScoreParams sp{static_cast<int>(B), static_cast<int>(Ns), static_cast<int>(Nd), static_cast<int>(Cp),
                  na, rinv, ci, cv, status, wait_budget_ns()};
-  dim3 sg(static_cast<unsigned>((Ns + kTM - 1) / kTM), static_cast<unsigned>(B));
+  // persistent: one CTA per SM over the (128-row block, batch row) items
+  int score_dev = 0, score_sms = 0;
+  SAF_CUDA_TRY(cudaGetDevice(&score_dev));
+  SAF_CUDA_TRY(cudaDeviceGetAttribute(&score_sms, cudaDevAttrMultiProcessorCount, score_dev));
+  const int64_t score_items = ((Ns + kTM - 1) / kTM) * B;
+  const dim3 sg(static_cast<unsigned>(std::min<int64_t>(score_items, score_sms)));
   // narrow metrics (per-head [k, |k|, v, |v|]) keep A resident; wide ones stream it
   const bool res = Cp / kTK <= kResChunks;
   auto launch = [&](auto kern, int smem) -> cudaError_t {

@@ -1285,6 +1285,7 @@ __global__ void __launch_bounds__(256) tome_kv_metric_kernel(const KvMetricParam
     const int n = n_first + r;
     if (n >= N) break;
     T* o = static_cast<T*>(p.out) + (static_cast<int64_t>(g) * N + n) * C;
+    uint32_t nrm_bits[2];
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
       double acc = 0.0;
@@ -1295,19 +1296,32 @@ __global__ void __launch_bounds__(256) tome_kv_metric_kernel(const KvMetricParam
           const T* e = reinterpret_cast<const T*>(&w[r][part][i]);
           const double a = static_cast<double>(to_f(e[0])), c = static_cast<double>(to_f(e[1]));
           acc = __dadd_rn(acc, __dadd_rn(__dmul_rn(a, a), __dmul_rn(c, c)));
-          T* od = o + part * (p.D + 1) + 2 * word;
-          od[0] = e[0];
-          od[1] = e[1];
         }
       }
 #pragma unroll
       for (int m = 16; m >= 1; m >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-      if (lane == 0) {
-        const double nrm = sqrt(acc);
-        if constexpr (std::is_same<T, __nv_bfloat16>::value) o[part * (p.D + 1) + p.D] = __double2bfloat16(nrm);
-        else o[part * (p.D + 1) + p.D] = __double2half(nrm);
-      }
+      const double nrm = sqrt(acc);
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) nrm_bits[part] = __bfloat16_as_ushort(__double2bfloat16(nrm));
+      else nrm_bits[part] = __half_as_ushort(__double2half(nrm));
     }
+    // The row [k (D), |k|, v (D), |v|] as 4-byte words (rows are 4-byte
+    // aligned, C = 2D + 2 is even): words [0, W) are k as loaded, word W is
+    // (|k|, v0), words W + 1 + i are (v[2i+1], v[2i+2]) -- v shifted by one
+    // 16-bit place, taken from this lane's word and the next one -- and word
+    // 2W is (v[D-1], |v|).
+    uint32_t* o32 = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int word = lane + 32 * i;
+      if (word < W) o32[word] = w[r][0][i];
+      const uint32_t cur = w[r][1][i];
+      uint32_t nxt = __shfl_down_sync(0xffffffffu, cur, 1);
+      const uint32_t wrap = __shfl_sync(0xffffffffu, w[r][1][i + 1 < 2 ? i + 1 : i], 0);
+      if (lane == 31) nxt = wrap;
+      if (word < W - 1) o32[W + 1 + word] = (cur >> 16) | (nxt << 16);
+      if (word == W - 1) o32[2 * W] = (cur >> 16) | (nrm_bits[1] << 16);
+    }
+    if (lane == 0) o32[W] = nrm_bits[0] | (w[r][1][0] << 16);
   }
 }
 }  // namespace

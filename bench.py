@@ -884,10 +884,11 @@ def bench_long(args, dev, world, rank):
     """long video (25 x 30 x 45 + 226 text, S = 33976),
     B = 2, H = 30, D = 64, bf16, 10% of 128-blocks.  Every rank holds a
     sequence shard [B, S/N, H, D] of q / k / v; UlyssesAttention packs it,
-    exchanges it with one NCCL all-to-all (heads split 4,4,4,4,4,4,3,3 at
-    N = 8), selects blocks and runs the block-sparse kernel on its heads, and
-    sends the output rows back (second all-to-all).  Strong scaling: the
-    layer is fixed, N GPUs share it."""
+    exchanges it with NCCL all-to-alls (heads split 4,4,4,4,4,4,3,3 at N = 8,
+    sent in head chunks whose exchanges overlap the previous chunk's compute),
+    selects blocks and runs the block-sparse kernel on its heads, and sends
+    the output rows back.  Strong scaling: the layer is fixed, N GPUs share
+    it."""
     import torch
 
     from sparseattnfunctions_b200 import kernels, workloads
@@ -902,13 +903,23 @@ def bench_long(args, dev, world, rank):
     q, k, v = (t.transpose(1, 2)[:, at:at + lens[rank]].contiguous().to(dev) for t in full)
     del full
     inner = BlockSparseAttention(block_size=128, density=0.10, geometry=geo)
-    ua = UlyssesAttention(inner, heads=H, seq_lens=lens)
+    live_acc, counting = [0.0], [True]
+
+    def counted(qh, kh, vh, out=None):  # live FLOP of every head chunk (warm-up calls only)
+        res = inner(qh, kh, vh, out=out)
+        if counting[0]:
+            live_acc[0] += float(inner.last_csr.live_flops(S, S, D))
+        return res
+
+    ua = UlyssesAttention(counted, heads=H, seq_lens=lens, chunks=args.ulysses_chunks)
     stream = torch.cuda.current_stream(dev)
     for _ in range(3):
+        live_acc[0] = 0.0
         ua(q, k, v)
     torch.cuda.synchronize()
     h = ua.local_heads
-    live = float(inner.last_csr.live_flops(S, S, D)) if h > 0 else 0.0
+    live = live_acc[0] if h > 0 else 0.0
+    counting[0] = False
     live_total = allreduce(live, "sum", world)
     n = max(3, min(args.long_steps, args.steps))
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
@@ -941,7 +952,8 @@ def bench_long(args, dev, world, rank):
     return {
         "workload": "config5: S=33976 (25x30x45 + 226 text), B=2, H=30, D=64, bf16, 10% of 128-blocks; "
                     f"sequence-sharded over {world} GPU(s), Ulysses all-to-all (NCCL) to "
-                    f"{kernels.head_split(H, world)} head ranges and back",
+                    f"{kernels.head_split(H, world)} head ranges and back, "
+                    f"in {len(ua.plan) if world > 1 else 1} pipelined head chunk(s)",
         "ms_per_layer": round(ms, 4), "ms_attention_only": round(ms_attn, 4),
         "live_tflop": round(live_total / 1e12, 4),
         "effective_tflops": round(live_total / (ms * 1e-3) / 1e12, 1),
@@ -1027,6 +1039,8 @@ def main():
     ap.add_argument("--combined-steps", type=int, default=2)
     ap.add_argument("--no-long", action="store_true", help="skip the config-5 sequence-sharded sub-benchmark")
     ap.add_argument("--long-steps", type=int, default=10)
+    ap.add_argument("--ulysses-chunks", type=int, default=3,
+                    help="head chunks of the config-5 exchange pipeline (1: one exchange each way)")
     ap.add_argument("--no-local-global", action="store_true", help="skip the LocalGlobalAttention sub-benchmark")
     ap.add_argument("--no-reference-kernel", action="store_true",
                     help="skip timing the reference's own Triton kernels (baseline/_ref) at N=1")

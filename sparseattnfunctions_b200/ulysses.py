@@ -24,6 +24,13 @@ exchange and no pack: the kernels read ``[B, S, H, D]`` in place as strided
 ``[B, H, S, D]`` views and write the output rows in place.  The reference
 itself is single-GPU.
 
+With ``chunks`` > 1 the heads go in chunks that pipeline: chunk c holds
+heads [C_c, C_c+1) split over the ranks (every rank keeps its head count of
+the contiguous split), and while the selection and attention of chunk c run,
+the all-to-alls of chunk c + 1's inputs and of chunk c - 1's outputs are in
+flight (asynchronous NCCL collectives on their own stream, waited for on the
+compute stream only where their data is used).
+
 ``pack`` / ``unpack`` / ``all_to_all`` default to the library kernels and
 ``torch.distributed``; tests inject host versions to check the exchange
 logic with the gloo backend on CPU.
@@ -38,18 +45,42 @@ import torch.distributed as dist
 from . import kernels
 
 
-def _default_all_to_all(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group) -> None:
-    dist.all_to_all_single(out, inp, output_split_sizes=list(out_splits),
-                           input_split_sizes=list(in_splits), group=group)
+def _default_all_to_all(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group):
+    """Asynchronous all-to-all; the returned work's ``wait()`` orders the
+    current stream after it."""
+    return dist.all_to_all_single(out, inp, output_split_sizes=list(out_splits),
+                                  input_split_sizes=list(in_splits), group=group, async_op=True)
+
+
+def chunk_plan(H: int, P: int, chunks: int) -> list:
+    """Head chunks of the pipelined exchange: a list of ``(c0, offs)`` with
+    chunk c = heads [c0, c0 + offs[-1]) and rank j's share of it
+    [c0 + offs[j], c0 + offs[j + 1]).  Rank j's shares add up to its count in
+    the contiguous split ``head_split(H, P)``."""
+    per_rank = kernels.head_split(H, P)
+    counts = [per_rank[j + 1] - per_rank[j] for j in range(P)]
+    plan, c0 = [], 0
+    for c in range(max(1, chunks)):
+        offs = [0]
+        for n in counts:
+            base, extra = divmod(n, max(1, chunks))
+            offs.append(offs[-1] + base + (1 if c < extra else 0))
+        if offs[-1] > 0:
+            plan.append((c0, offs))
+        c0 += offs[-1]
+    return plan
 
 
 class UlyssesAttention:
     def __init__(self, inner: Callable, heads: int, group=None, seq_lens: Optional[Sequence[int]] = None,
                  pack: Optional[Callable] = None, unpack: Optional[Callable] = None,
-                 all_to_all: Optional[Callable] = None):
+                 all_to_all: Optional[Callable] = None, chunks: int = 3):
         """``inner(q, k, v, out=o)`` computes attention of ``[B, h, S, D]``
         (strided) views into ``o``; ``heads`` is the total head count H;
-        ``seq_lens`` the per-rank shard lengths (default: equal shards)."""
+        ``seq_lens`` the per-rank shard lengths (default: equal shards);
+        ``chunks`` the head chunks of the pipelined exchange.  An injected
+        ``all_to_all`` may run synchronously (return None) or return a work
+        with ``wait()``."""
         self.inner = inner
         self.heads = heads
         self.group = group
@@ -59,6 +90,7 @@ class UlyssesAttention:
             self.world, self.rank = 1, 0
         self.seq_lens = list(seq_lens) if seq_lens is not None else None
         self.head_off = kernels.head_split(heads, self.world)
+        self.plan = chunk_plan(heads, self.world, chunks)
         self.pack = pack or (lambda ts, off: kernels.ulysses_pack(ts, off))
         self.unpack = unpack or kernels.ulysses_unpack
         self.all_to_all = all_to_all or _default_all_to_all
@@ -79,7 +111,6 @@ class UlyssesAttention:
         S = sum(lens)
         off = self.head_off
         h = off[r + 1] - off[r]
-        hs = [off[j + 1] - off[j] for j in range(P)]
         if P == 1:
             # one rank holds every head and the whole sequence: the kernels
             # read the [B, S, H, D] inputs as strided [B, H, S, D] views and
@@ -88,20 +119,39 @@ class UlyssesAttention:
             self.inner(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), out=out.transpose(1, 2))
             self.last = {"S": S, "local_heads": H, "send_elems": 0, "recv_elems": 0}
             return out
-        send = self.pack([q, k, v], off)
-        recv = torch.empty(S * B * 3 * h * D, dtype=q.dtype, device=q.device)
-        self.all_to_all(recv, send, [n * B * 3 * h * D for n in lens], [s * B * 3 * hj * D for hj in hs],
-                        self.group)
-        grid = recv[:S * B * 3 * h * D].view(S, B, 3, h, D)
-        qh, kh, vh = (grid[:, :, t].permute(1, 2, 0, 3) for t in range(3))
-        o_rows = torch.empty(S, B, h, D, dtype=q.dtype, device=q.device)
-        oh = o_rows.permute(1, 2, 0, 3)
-        if h > 0:
-            self.inner(qh, kh, vh, out=oh)
-        back = torch.empty(s * B * H * D, dtype=q.dtype, device=q.device)
-        self.all_to_all(back, o_rows.view(-1), [s * B * hj * D for hj in hs], [n * B * h * D for n in lens],
-                        self.group)
+        # inputs of every chunk packed and sent up front (the collectives
+        # run in order on the communication stream)
+        sends = []
+        for c0, offs in self.plan:
+            hc = offs[-1]  # the chunk's heads; this rank's share h_c
+            h_c = offs[r + 1] - offs[r]
+            hs_c = [offs[j + 1] - offs[j] for j in range(P)]
+            send = self.pack([t[:, :, c0:c0 + hc] for t in (q, k, v)], offs)
+            recv = torch.empty(S * B * 3 * h_c * D, dtype=q.dtype, device=q.device)
+            work = self.all_to_all(recv, send, [n * B * 3 * h_c * D for n in lens],
+                                   [s * B * 3 * hj * D for hj in hs_c], self.group)
+            sends.append((c0, hc, offs, h_c, hs_c, send, recv, work))
+        backs = []
+        send_elems = recv_elems = 0
+        for c0, hc, offs, h_c, hs_c, send, recv, work in sends:
+            if work is not None:
+                work.wait()
+            send_elems += send.numel()
+            recv_elems += recv.numel()
+            grid = recv.view(S, B, 3, h_c, D)
+            qh, kh, vh = (grid[:, :, t].permute(1, 2, 0, 3) for t in range(3))
+            o_rows = torch.empty(S, B, h_c, D, dtype=q.dtype, device=q.device)
+            if h_c > 0:
+                self.inner(qh, kh, vh, out=o_rows.permute(1, 2, 0, 3))
+            back = torch.empty(s * B * hc * D, dtype=q.dtype, device=q.device)
+            wb = self.all_to_all(back, o_rows.view(-1), [s * B * hj * D for hj in hs_c],
+                                 [n * B * h_c * D for n in lens], self.group)
+            backs.append((c0, hc, offs, back, o_rows, wb))
         out = torch.empty(B, s, H, D, dtype=q.dtype, device=q.device)
-        self.unpack(back, [out], off)
-        self.last = {"S": S, "local_heads": h, "send_elems": send.numel(), "recv_elems": recv.numel()}
+        for c0, hc, offs, back, o_rows, wb in backs:
+            if wb is not None:
+                wb.wait()
+            self.unpack(back, [out[:, :, c0:c0 + hc]], offs)
+        self.last = {"S": S, "local_heads": h, "send_elems": send_elems, "recv_elems": recv_elems,
+                     "chunks": len(self.plan)}
         return out

@@ -36,7 +36,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, lens, result_q):
+def _worker(rank, world, port, lens, chunks, result_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     from datetime import timedelta
@@ -48,19 +48,20 @@ def _worker(rank, world, port, lens, result_q):
         q, k, v = _inputs(sum(lens))
         at = sum(lens[:rank])
         shard = [t[:, at:at + lens[rank]].contiguous() for t in (q, k, v)]
-        ua = UlyssesAttention(_dense, heads=H, seq_lens=lens, pack=oul.pack, unpack=oul.unpack)
+        ua = UlyssesAttention(_dense, heads=H, seq_lens=lens, pack=oul.pack, unpack=oul.unpack, chunks=chunks)
         out = ua(*shard)
         result_q.put((rank, out.numpy(), ua.local_heads))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("lens", [[24, 24], [17, 31]])
-def test_ulysses_two_gloo_ranks(lens):
+@pytest.mark.parametrize("lens,chunks", [([24, 24], 1), ([17, 31], 2), ([24, 24], 3)])
+def test_ulysses_two_gloo_ranks(lens, chunks):
+    """Single exchange (chunks = 1) and the head-chunked pipeline."""
     ctx = mp.get_context("spawn")
     result_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, lens, result_q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, lens, chunks, result_q)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}
@@ -95,3 +96,22 @@ def test_pack_unpack_roundtrip_and_layout():
     outs = [torch.zeros_like(t) for t in ts]
     oul.unpack(buf, outs, off)
     assert all(torch.equal(a, b) for a, b in zip(outs, ts))
+
+
+def test_chunk_plan_keeps_each_ranks_head_count():
+    from sparseattnfunctions_b200.kernels import head_split
+    from sparseattnfunctions_b200.ulysses import chunk_plan
+
+    for H, P, C in ((30, 8, 2), (30, 2, 2), (5, 2, 3), (30, 4, 4), (3, 8, 2)):
+        plan = chunk_plan(H, P, C)
+        off = head_split(H, P)
+        per_rank = [0] * P
+        c_prev = 0
+        for c0, offs in plan:
+            assert c0 == c_prev and offs[0] == 0 and offs[-1] > 0
+            c_prev = c0 + offs[-1]
+            for j in range(P):
+                per_rank[j] += offs[j + 1] - offs[j]
+        assert c_prev == H
+        assert per_rank == [off[j + 1] - off[j] for j in range(P)]
+    assert chunk_plan(30, 2, 2) == [(0, [0, 8, 16]), (16, [0, 7, 14])]

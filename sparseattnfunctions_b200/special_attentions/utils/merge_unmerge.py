@@ -64,8 +64,18 @@ def video_split(w: int, h: int, t: int, sx: int, sy: int, st: int, device,
         full = torch.zeros(tt, h, w, dtype=torch.int64, device=device)
         full[:tst * st, :hsy * sy, :wsx * sx] = buf
         buf = full
-    order = torch.argsort(buf.reshape(-1), stable=True) + w * h
+    # the stable argsort of the {-1, 0} buffer is a stable partition (the one
+    # dst token of every cell first, in token order, then the src tokens):
+    # two prefix counts and a scatter instead of a device radix sort
+    flat = buf.reshape(-1)
+    n = flat.numel()
     num_dst = tst * hsy * wsx
+    is_dst = flat < 0
+    c_dst = torch.cumsum(is_dst, 0)
+    pos = torch.where(is_dst, c_dst - 1, num_dst + torch.arange(n, device=device) - c_dst)
+    order = torch.empty(n, dtype=torch.int64, device=device)
+    order.scatter_(0, pos, torch.arange(n, dtype=torch.int64, device=device))
+    order += w * h
     a_idx = order[num_dst:]
     b_idx = torch.cat([torch.arange(w * h, device=device), order[:num_dst]])
     return a_idx.to(torch.int32), b_idx.to(torch.int32)

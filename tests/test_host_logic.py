@@ -78,3 +78,35 @@ def test_cpu_tensors_are_refused():
     q = torch.zeros(1, 1, 128, 64, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         kernels.pool_topk(q, q, block_m=128, block_n=128, topk=1)
+
+
+def test_video_split_is_the_stable_argsort_partition():
+    """merge_unmerge.py:52-67 orders the video tokens by a stable argsort of
+    a {-1 (dst), 0 (src)} buffer; the mirror's prefix-count partition gives
+    the same (a_idx, b_idx) for random and fixed dst picks, with and
+    without a ragged border."""
+    import torch
+
+    from sparseattnfunctions_b200.special_attentions.utils import merge_unmerge as mu
+
+    def by_argsort(w, h, t, sx, sy, st, rand_idx):
+        tt = t - 1
+        hsy, wsx, tst = h // sy, w // sx, tt // st
+        if rand_idx is None:
+            rand_idx = torch.zeros(tst, hsy, wsx, 1, dtype=torch.int64)
+        buf = torch.zeros(tst, hsy, wsx, st * sy * sx, dtype=torch.int64)
+        buf.scatter_(3, rand_idx.reshape(tst, hsy, wsx, 1), -torch.ones(tst, hsy, wsx, 1, dtype=torch.int64))
+        buf = buf.view(tst, hsy, wsx, st, sy, sx).permute(0, 3, 1, 4, 2, 5).reshape(tst * st, hsy * sy, wsx * sx)
+        full = torch.zeros(tt, h, w, dtype=torch.int64)
+        full[:tst * st, :hsy * sy, :wsx * sx] = buf
+        order = torch.argsort(full.reshape(-1), stable=True) + w * h
+        n_dst = tst * hsy * wsx
+        return order[n_dst:].to(torch.int32), torch.cat([torch.arange(w * h), order[:n_dst]]).to(torch.int32)
+
+    g = torch.Generator().manual_seed(0)
+    for w, h, t, sx, sy, st in [(45, 30, 13, 2, 2, 1), (45, 30, 13, 3, 2, 2), (7, 5, 4, 2, 2, 1), (9, 9, 6, 2, 3, 2)]:
+        tst, hsy, wsx = (t - 1) // st, h // sy, w // sx
+        for rnd in (None, torch.randint(st * sy * sx, (tst, hsy, wsx, 1), generator=g)):
+            a_ref, b_ref = by_argsort(w, h, t, sx, sy, st, rnd)
+            a, b = mu.video_split(w, h, t, sx, sy, st, "cpu", rnd)
+            assert torch.equal(a, a_ref) and torch.equal(b, b_ref)

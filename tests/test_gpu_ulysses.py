@@ -90,3 +90,47 @@ def test_emulated_ranks_match_plain_processor(cuda_device, P):
         out = torch.empty(2, lens[r], H, D, dtype=q.dtype, device=cuda_device)
         kernels.ulysses_unpack(back, [out], off)
         assert torch.equal(out, want[:, starts[r]:starts[r] + lens[r]])
+
+
+@pytest.mark.parametrize("P,chunks", [(2, 3), (4, 2)])
+def test_emulated_chunked_exchange_matches_plain_processor(cuda_device, P, chunks):
+    """The head-chunked exchange of UlyssesAttention emulated for P ranks on
+    one GPU: per chunk, pack the head-slice views of every shard, route the
+    chunks, attention on the strided views, route the rows back and unpack
+    into the head-slice view of each rank's output."""
+    from sparseattnfunctions_b200.ulysses import chunk_plan
+
+    H, D = 5, 64
+    q, k, v = _full_inputs(cuda_device, H, D, seed=10 + P)
+    S = q.shape[1]
+    lens = [S // P + (1 if r < S % P else 0) for r in range(P)]
+    starts = [sum(lens[:r]) for r in range(P)]
+    inner = BlockSparseAttention(block_size=64, density=0.3, geometry=GEOM)
+    want = inner(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
+    outs = [torch.empty(2, lens[r], H, D, dtype=q.dtype, device=cuda_device) for r in range(P)]
+
+    def chunk(buf, sizes, j):
+        a = sum(sizes[:j])
+        return buf[a:a + sizes[j]]
+
+    for c0, offs in chunk_plan(H, P, chunks):
+        hc = offs[-1]
+        hs = [offs[j + 1] - offs[j] for j in range(P)]
+        sends = [kernels.ulysses_pack([t[:, starts[r]:starts[r] + lens[r], c0:c0 + hc] for t in (q, k, v)], offs)
+                 for r in range(P)]
+        rows = []
+        for r in range(P):
+            recv = torch.cat([chunk(sends[i], [lens[i] * 2 * 3 * hj * D for hj in hs], r) for i in range(P)])
+            o_rows = torch.empty(S, 2, hs[r], D, dtype=q.dtype, device=cuda_device)
+            if hs[r] > 0:
+                grid = recv.view(S, 2, 3, hs[r], D)
+                qh, kh, vh = (grid[:, :, t].permute(1, 2, 0, 3) for t in range(3))
+                inner(qh, kh, vh, out=o_rows.permute(1, 2, 0, 3))
+            rows.append(o_rows.view(-1))
+        for r in range(P):
+            back = torch.cat([chunk(rows[j], [n * 2 * hs[j] * D for n in lens], r) for j in range(P)])
+            kernels.ulysses_unpack(back, [outs[r][:, :, c0:c0 + hc]], offs)
+    for r in range(P):
+        ref = want[:, starts[r]:starts[r] + lens[r]]
+        assert torch.equal(outs[r].isnan(), ref.isnan())
+        assert float((outs[r].float() - ref.float()).nan_to_num().abs().max()) <= 2e-2

@@ -52,10 +52,10 @@ struct PoolOperand {
 // block barrier, so the many small blocks cost no per-CTA synchronisation.
 // grid (ceil(B*H*max nb / 8), 1, 2): z = 0 pools q, z = 1 pools k.
 template <typename T>
-__global__ void __launch_bounds__(256, 3) pool_mean_warp_kernel(PoolOperand q_op, PoolOperand k_op, int H,
+__global__ void __launch_bounds__(256, 2) pool_mean_warp_kernel(PoolOperand q_op, PoolOperand k_op, int H,
                                                              int D, int BH, int lpr_log2) {
   constexpr int VEC = 16 / sizeof(T);
-  constexpr int U = 6;  // row loads in flight per lane
+  constexpr int U = 8;  // row loads in flight per lane (6 at three CTAs per SM: 1 us slower at 8 heads)
   const PoolOperand& op = blockIdx.z == 0 ? q_op : k_op;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + warp;
@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(kPoolThreads) pool_mean_kernel(PoolOperand q_o
 
 struct SelectArgs {
   int nbq, nbk, D;
+  int dc;  // dimensions staged per pass (divides D)
   int topk, text_q, text_k, force_diag, forced_inside;
   const double* qbar;  // [BH, nbq, D]
   const double* kbar;  // [BH, nbk, D]
@@ -159,153 +160,191 @@ struct SelectArgs {
   double* score_out;   // nullable [BH, nbq, nbk]
 };
 
-__device__ __forceinline__ bool better(double a, int ia, double b, int ib) {
-  return a > b || (a == b && ia < ib);
+// 16-byte asynchronous global -> shared copy, cached in L2 only.
+__device__ __forceinline__ void cp_async16(double* dst, const double* src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+// Order-preserving 64-bit key of a score: larger score <-> larger key, -0.0
+// keyed as +0.0 (the two compare equal), 0 reserved for "not a candidate"
+// (NaN, which never compares higher, and columns outside the top-k pool).
+// Every finite or infinite score keys to at least 0x000FFFFFFFFFFFFF, so a
+// candidate's high word is never 0.
+__device__ __forceinline__ unsigned long long score_key(double s, bool candidate) {
+  const double c = __dadd_rn(s, 0.0);  // -0.0 + 0.0 == +0.0; any other value unchanged
+  const unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(c));
+  if (!candidate || c != c) return 0ull;
+  return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
 }
 
 // grid (B*H, ceil(nbq / (8 RPW))), 256 threads; each warp owns RPW
-// consecutive row blocks, so every key mean staged in shared memory (32 dims
-// at a time) serves RPW rows: two when the grid fills the GPU (the staged
-// means serve twice the rows), one when few heads share a GPU (twice the
-// CTAs, and the serial top-k rounds of a warp cover half the rows).  Every
-// lane owns columns lane + 32m (m < M) and accumulates their fp64 scores
-// with d ascending (separate multiply and add, no contraction).  The top-k
-// is k rounds of a warp arg-max (ties -> lower column).
+// consecutive row blocks.  The head's key means and the CTA's query means
+// are staged in shared memory dc dimensions at a time (dc = D whenever both
+// fit in ~100 KB, two CTAs per SM) by 16-byte cp.async copies, all in flight
+// at once, into rows of dc + 2 doubles: a lane's 16-byte read of (d, d + 1)
+// then falls in a different bank group for each of 8 consecutive rows, so a
+// warp's read of 32 columns is conflict-free.  Every lane owns columns
+// lane + 32m (m < M) and accumulates their fp64 scores with d ascending
+// (separate multiply and add, no contraction); one shared-memory read of a
+// key pair serves RPW rows.  Lanes past the last column read the last
+// column's row (their scores are never candidates).
+//
+// The top-k is k rounds of a warp arg-max over order-preserving 64-bit keys
+// of the scores, the RPW rows of a warp advancing together: redux.sync max of
+// the lanes' best high words, and a ballot of the lanes holding it; when one
+// lane holds it, that lane's best is the winner, otherwise the low words and
+// then the lowest column among equal keys decide.  Only the lane that owned
+// the winner rescans its columns.
 template <int M, int RPW>
 __global__ void __launch_bounds__(256) score_topk_kernel(const SelectArgs a) {
-  constexpr int kRowsPerWarp = RPW;
   constexpr int kRowsPerCta = 8 * RPW;
-  extern __shared__ double ks[];  // [nbk][kDChunk+1] then [32][kDChunk+1]
-  double* qs = ks + a.nbk * (kDChunk + 1);
+  extern __shared__ __align__(16) double ks[];  // [nbk][dc + 2] then [kRowsPerCta][dc + 2]
+  const int dc = a.dc, ld = a.dc + 2, half = a.dc >> 1;
+  double* qs = ks + a.nbk * ld;
   const int g = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.y * kRowsPerCta + warp * kRowsPerWarp;
+  const int cta_row0 = blockIdx.y * kRowsPerCta;
+  const int row0 = cta_row0 + warp * RPW;
+  const int qrows = min(kRowsPerCta, a.nbq - cta_row0);
 
-  double sc[kRowsPerWarp][M];
+  double sc[RPW][M];
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i)
+  for (int i = 0; i < RPW; ++i)
 #pragma unroll
     for (int m = 0; m < M; ++m) sc[i][m] = 0.0;
+  int koff[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) koff[m] = min(lane + 32 * m, a.nbk - 1) * ld;
 
   const double* kb = a.kbar + static_cast<int64_t>(g) * a.nbk * a.D;
-  const double* qb = a.qbar + static_cast<int64_t>(g) * a.nbq * a.D;
-  // staging: every thread issues its loads 8 at a time before storing them
-  // (a few memory round trips per chunk instead of one per element)
-  constexpr int kKLoads = (32 * M * kDChunk + 255) / 256;
-  constexpr int kQLoads = (kRowsPerCta * kDChunk + 255) / 256;
-  for (int d0 = 0; d0 < a.D; d0 += kDChunk) {
+  const double* qb = a.qbar + (static_cast<int64_t>(g) * a.nbq + cta_row0) * a.D;
+  const double* qr = qs + warp * RPW * ld;
+  for (int d0 = 0; d0 < a.D; d0 += dc) {
+    if (d0 > 0) __syncthreads();  // every warp is done with the previous pass
+    for (int j = warp; j < a.nbk; j += 8)
+      for (int c = lane; c < half; c += 32)
+        cp_async16(ks + j * ld + 2 * c, kb + static_cast<int64_t>(j) * a.D + d0 + 2 * c);
+    for (int r = warp; r < qrows; r += 8)
+      for (int c = lane; c < half; c += 32)
+        cp_async16(qs + r * ld + 2 * c, qb + static_cast<int64_t>(r) * a.D + d0 + 2 * c);
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-#pragma unroll 1
-    for (int u0 = 0; u0 < kKLoads; u0 += 8) {
-      double kt[8];
+#pragma unroll 2
+    for (int d = 0; d < dc; d += 2) {
+      double2 qv[RPW];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int idx = threadIdx.x + 256 * (u0 + u);
-        const int j = idx / kDChunk, d = idx % kDChunk;
-        kt[u] = (u0 + u < kKLoads && j < a.nbk) ? kb[static_cast<int64_t>(j) * a.D + d0 + d] : 0.0;
-      }
+      for (int i = 0; i < RPW; ++i) qv[i] = *reinterpret_cast<const double2*>(qr + i * ld + d);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int idx = threadIdx.x + 256 * (u0 + u);
-        const int j = idx / kDChunk, d = idx % kDChunk;
-        if (u0 + u < kKLoads && j < a.nbk) ks[j * (kDChunk + 1) + d] = kt[u];
-      }
-      asm volatile("" ::: "memory");  // keep the next group's loads after these stores
-    }
-    {
-      double qt[kQLoads];
+      for (int m = 0; m < M; ++m) {
+        const double2 kv = *reinterpret_cast<const double2*>(ks + koff[m] + d);
 #pragma unroll
-      for (int u = 0; u < kQLoads; ++u) {
-        const int idx = threadIdx.x + 256 * u;
-        const int r = idx / kDChunk, d = idx % kDChunk;
-        const int rr = blockIdx.y * kRowsPerCta + r;
-        qt[u] = rr < a.nbq ? qb[static_cast<int64_t>(rr) * a.D + d0 + d] : 0.0;
-      }
-#pragma unroll
-      for (int u = 0; u < kQLoads; ++u) {
-        const int idx = threadIdx.x + 256 * u;
-        qs[(idx / kDChunk) * (kDChunk + 1) + idx % kDChunk] = qt[u];
-      }
-    }
-    __syncthreads();
-    const double* qr = qs + warp * kRowsPerWarp * (kDChunk + 1);
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const int j = lane + 32 * m;
-      if (j < a.nbk) {
-        const double* kr = ks + j * (kDChunk + 1);
-#pragma unroll 4
-        for (int d = 0; d < kDChunk; ++d) {
-          const double kv = kr[d];
-#pragma unroll
-          for (int i = 0; i < kRowsPerWarp; ++i)
-            sc[i][m] = __dadd_rn(sc[i][m], __dmul_rn(qr[i * (kDChunk + 1) + d], kv));
+        for (int i = 0; i < RPW; ++i) {
+          sc[i][m] = __dadd_rn(sc[i][m], __dmul_rn(qv[i].x, kv.x));
+          sc[i][m] = __dadd_rn(sc[i][m], __dmul_rn(qv[i].y, kv.y));
         }
       }
     }
   }
 
+  // Per row: forced / candidate columns, the keys, and the lane's best key.
+  uint32_t forced[RPW], sel[RPW];
+  int krem[RPW];
+  unsigned long long key[RPW][M], bk[RPW];
+  int bm[RPW];
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
+  for (int i = 0; i < RPW; ++i) {
     const int row = row0 + i;
-    if (row >= a.nbq) break;
-    const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
-    uint32_t forced = 0, eligible = 0, sel = 0;  // bit m <-> column lane + 32m
+    const bool live_row = row < a.nbq;
     const bool text_row = row < a.text_q;
+    uint32_t eligible = 0;
+    forced[i] = 0;
+    sel[i] = 0;
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       const int j = lane + 32 * m;
       if (j < a.nbk) {
         const bool f = text_row || j < a.text_k || (a.force_diag && j == row);
-        if (f) forced |= 1u << m;
+        if (f) forced[i] |= 1u << m;
         if (!(f && a.forced_inside)) eligible |= 1u << m;
       }
     }
     int nforced = 0;
 #pragma unroll
-    for (int m = 0; m < M; ++m) nforced += __popc(__ballot_sync(0xffffffffu, (forced >> m) & 1u));
-    int krem = a.forced_inside ? a.topk - nforced : a.topk;
-    if (text_row) krem = 0;
-    for (int round = 0; round < krem; ++round) {
-      double best = -INFINITY;
-      int bj = 0x7fffffff;
+    for (int m = 0; m < M; ++m) nforced += __popc(__ballot_sync(0xffffffffu, (forced[i] >> m) & 1u));
+    krem[i] = a.forced_inside ? a.topk - nforced : a.topk;
+    if (text_row || !live_row) krem[i] = 0;
+    if (live_row && a.score_out) {
+      const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        if (((eligible & ~sel) >> m) & 1u) {
-          const int j = lane + 32 * m;
-          if (better(sc[i][m], j, best, bj)) {
-            best = sc[i][m];
-            bj = j;
-          }
-        }
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const double ob = __shfl_xor_sync(0xffffffffu, best, off);
-        const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
-        if (better(ob, oj, best, bj)) {
-          best = ob;
-          bj = oj;
-        }
-      }
-      if (bj == 0x7fffffff) break;  // no candidate left
-      if ((bj & 31) == lane) sel |= 1u << (bj >> 5);
+      for (int m = 0; m < M; ++m)
+        if (lane + 32 * m < a.nbk) a.score_out[rbase + lane + 32 * m] = sc[i][m];
     }
-    sel |= forced;
+    bk[i] = 0ull;
+    bm[i] = 0;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      key[i][m] = score_key(sc[i][m], (eligible >> m) & 1u);
+      if (key[i][m] > bk[i]) {
+        bk[i] = key[i][m];
+        bm[i] = m;
+      }
+    }
+  }
+  int kmax = 0;
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) kmax = max(kmax, krem[i]);
+  for (int round = 0; round < kmax; ++round) {
+    uint32_t hi[RPW], holders[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) hi[i] = __reduce_max_sync(0xffffffffu, static_cast<uint32_t>(bk[i] >> 32));
+#pragma unroll
+    for (int i = 0; i < RPW; ++i)
+      holders[i] = __ballot_sync(0xffffffffu, static_cast<uint32_t>(bk[i] >> 32) == hi[i]);
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      if (round >= krem[i] || hi[i] == 0u) continue;  // row done, or no candidate left (uniform)
+      bool win;
+      if (__popc(holders[i]) == 1) {
+        win = lane == __ffs(holders[i]) - 1;
+      } else {
+        const bool top = (holders[i] >> lane) & 1u;
+        const uint32_t lo = __reduce_max_sync(0xffffffffu, top ? static_cast<uint32_t>(bk[i]) : 0u);
+        const bool hold = top && static_cast<uint32_t>(bk[i]) == lo;
+        const uint32_t col =
+            __reduce_min_sync(0xffffffffu, hold ? static_cast<uint32_t>(lane + 32 * bm[i]) : 0xffffffffu);
+        win = (col & 31u) == static_cast<uint32_t>(lane);
+      }
+      if (win) {
+        sel[i] |= 1u << bm[i];
+        bk[i] = 0ull;
+        bm[i] = 0;
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+          if (!((sel[i] >> m) & 1u) && key[i][m] > bk[i]) {
+            bk[i] = key[i][m];
+            bm[i] = m;
+          }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int row = row0 + i;
+    if (row >= a.nbq) break;
+    const int64_t rbase = (static_cast<int64_t>(g) * a.nbq + row) * a.nbk;
+    const uint32_t s = sel[i] | forced[i];
     int base = 0;
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-      const uint32_t bal = __ballot_sync(0xffffffffu, (sel >> m) & 1u);
-      if ((sel >> m) & 1u) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (s >> m) & 1u);
+      if ((s >> m) & 1u) {
         const int pos = base + __popc(bal & ((1u << lane) - 1u));
         a.padded[rbase + pos] = lane + 32 * m;
       }
       base += __popc(bal);
-      const int j = lane + 32 * m;
-      if (j < a.nbk) {
-        if (a.mask_out) a.mask_out[rbase + j] = (sel >> m) & 1u;
-        if (a.score_out) a.score_out[rbase + j] = sc[i][m];
-      }
+      if (a.mask_out && lane + 32 * m < a.nbk) a.mask_out[rbase + lane + 32 * m] = (s >> m) & 1u;
     }
     if (lane == 0) a.counts[static_cast<int64_t>(g) * a.nbq + row] = base;
   }
@@ -477,9 +516,15 @@ int32_t pool_dispatch(const saf_tensor4* q, const saf_tensor4* k, int bm, int bn
 }
 
 template <int M, int RPW>
-int32_t launch_score_rpw(const SelectArgs& a, int64_t BH, cudaStream_t st) {
+int32_t launch_score_rpw(SelectArgs a, int64_t BH, cudaStream_t st) {
   constexpr int kRowsPerCta = 8 * RPW;
-  const size_t smem = (static_cast<size_t>(a.nbk) + kRowsPerCta) * (kDChunk + 1) * sizeof(double);
+  constexpr size_t kSmemTarget = 100 * 1024;  // two CTAs per SM
+  auto smem_of = [&](int dc) {
+    return (static_cast<size_t>(a.nbk) + kRowsPerCta) * (dc + 2) * sizeof(double);
+  };
+  a.dc = a.D;  // whole rows in one pass when they fit, else kDChunk (D % kDChunk == 0)
+  if (smem_of(a.dc) > kSmemTarget) a.dc = kDChunk;
+  const size_t smem = smem_of(a.dc);
   SAF_CUDA_TRY(cudaFuncSetAttribute(score_topk_kernel<M, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
   dim3 grid(static_cast<unsigned>(BH), (a.nbq + kRowsPerCta - 1) / kRowsPerCta);
@@ -487,16 +532,19 @@ int32_t launch_score_rpw(const SelectArgs& a, int64_t BH, cudaStream_t st) {
   return SAF_OK;
 }
 
-// Two rows a warp unless that grid leaves SMs without a CTA (measured at
-// CogVideoX-2B shape: 8 heads 37.0 -> 32.9 us with one row a warp, 30 heads
-// 68.7 -> 72.3 us, so the switch sits at one CTA per SM).
+// Two rows a warp unless that grid leaves SMs without a CTA.  Measured at the
+// CogVideoX-2B shape (139 x 139 blocks, B = 2): 4 heads 10.6 us, 30 heads
+// 38.3 us.  Four rows a warp (90 KB of shared memory, two CTAs per SM) was
+// slower at 15 and 30 heads (30.2 against 20.6 us at 15): with fewer CTAs
+// fewer warps hide the chains of dependent fp64 adds.
 template <int M>
 int32_t launch_score(const SelectArgs& a, int64_t BH, cudaStream_t st) {
   int dev = 0, sms = 0;
   SAF_CUDA_TRY(cudaGetDevice(&dev));
   SAF_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int64_t ctas2 = BH * ((a.nbq + 15) / 16);
-  return ctas2 >= sms ? launch_score_rpw<M, 2>(a, BH, st) : launch_score_rpw<M, 1>(a, BH, st);
+  auto ctas = [&](int rpw) { return BH * ((a.nbq + 8 * rpw - 1) / (8 * rpw)); };
+  if (ctas(2) >= sms) return launch_score_rpw<M, 2>(a, BH, st);
+  return launch_score_rpw<M, 1>(a, BH, st);
 }
 
 }  // namespace

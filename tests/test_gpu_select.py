@@ -93,3 +93,20 @@ def test_cogvideox_config2_selection(cuda_device):
                  tk=geo.text_blocks(128))
     nnz = csr.nnz_per_head().cpu()
     assert int(nnz.max()) <= 2 * nb + (nb - 2) * (topk + 2)
+
+
+@pytest.mark.parametrize("S,block,topk,tq,tk,diag,inside,d", [
+    (4096, 128, 8, 1, 1, False, False, 64),       # 32 key blocks, one row block a warp
+    (4096, 128, 8, 1, 2, True, True, 64),         # forced columns counted inside the k
+    (260 * 128, 128, 20, 2, 2, False, False, 64),  # 9 columns a lane
+    (400 * 64, 64, 30, 0, 0, True, False, 64),    # 16 columns a lane
+    (17776, 128, 14, 2, 2, False, False, 128),    # key means staged in two passes of 64 dims
+])
+def test_integer_inputs_many_ties(cuda_device, S, block, topk, tq, tk, diag, inside, d):
+    """Small-integer q / k make many block scores exactly equal (the means
+    are exact), so the top-k order among equal scores (lower column first)
+    decides most rows; bit-exact against the oracle."""
+    g = torch.Generator().manual_seed(S + d)
+    q = torch.randint(-2, 3, (1, 2, S, d), generator=g).to(torch.bfloat16)
+    k = torch.randint(-2, 3, (1, 2, S, d), generator=g).to(torch.bfloat16)
+    _check(cuda_device, q, k, block, block, topk, tq=tq, tk=tk, diag=diag, inside=inside)

@@ -60,7 +60,8 @@ def topk_select(scores: np.ndarray, topk: int, text_blocks_q: int = 0, text_bloc
     """Dense bool block mask [B,H,nbq,nbk] from pooled scores.
 
     Rows ``i < text_blocks_q`` are dense.  Other rows keep their top-k columns
-    (higher score first, equal scores -> lower column) united with the forced
+    (NaN first, as torch.topk ranks it, then higher score first; equal scores
+    and NaNs -> lower column) united with the forced
     columns (``j < text_blocks_k``; ``j == i`` with ``force_diag``).  With
     ``forced_inside_topk`` the forced columns count toward ``topk`` and the
     remaining ``topk - |forced|`` are chosen among the other columns.
@@ -86,8 +87,10 @@ def topk_select(scores: np.ndarray, topk: int, text_blocks_q: int = 0, text_bloc
         row = scores[:, :, i, :][..., elig]  # [B,H,n_elig]
         k = min(k, ecols.size)
         if k > 0:
-            # stable sort on -score keeps lower columns first among equal scores
-            order = np.argsort(-row, axis=-1, kind="stable")[..., :k]
+            # NaN first (torch.topk ranks NaN highest), then higher scores; the
+            # stable sort keeps lower columns first among equal scores and NaNs
+            nan = np.isnan(row)
+            order = np.lexsort((np.where(nan, 0.0, -row), ~nan), axis=-1)[..., :k]
             sel = ecols[order]
             np.put_along_axis(mask[:, :, i, :], sel, True, axis=-1)
         mask[:, :, i, forced] = True

@@ -9,7 +9,8 @@
 //     (IEEE division);
 //   * score[i][j] = sum_d q_mean[i][d] * k_mean[j][d] in fp64, d ascending,
 //     every product and every sum rounded separately (no FMA contraction);
-//   * top-k order: higher score first, equal scores -> lower column first.
+//   * top-k order: higher score first, equal scores -> lower column first,
+//     NaN above every number (torch.topk's rule; NaNs tie among themselves).
 // With these rules the GPU and the oracle select bit-identical blocks.
 //
 // Reference counterparts: calc_attn_block_sum_efficient
@@ -167,14 +168,16 @@ __device__ __forceinline__ void cp_async16(double* dst, const double* src) {
 }
 
 // Order-preserving 64-bit key of a score: larger score <-> larger key, -0.0
-// keyed as +0.0 (the two compare equal), 0 reserved for "not a candidate"
-// (NaN, which never compares higher, and columns outside the top-k pool).
-// Every finite or infinite score keys to at least 0x000FFFFFFFFFFFFF, so a
-// candidate's high word is never 0.
+// keyed as +0.0 (the two compare equal), NaN keyed above +inf (torch.topk,
+// which the reference selects with, ranks NaN highest; all NaNs tie, so the
+// lower column goes first), 0 reserved for columns outside the top-k pool.
+// Every candidate keys to at least 0x000FFFFFFFFFFFFF, so its high word is
+// never 0.
 __device__ __forceinline__ unsigned long long score_key(double s, bool candidate) {
   const double c = __dadd_rn(s, 0.0);  // -0.0 + 0.0 == +0.0; any other value unchanged
   const unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(c));
-  if (!candidate || c != c) return 0ull;
+  if (!candidate) return 0ull;
+  if (c != c) return ~0ull;
   return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
 }
 

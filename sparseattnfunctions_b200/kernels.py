@@ -116,7 +116,8 @@ def pool_topk(q: torch.Tensor, k: torch.Tensor, *, block_m: int, block_n: int, t
     """Block selection by mean-pooled scores (one launch sequence, no sync).
 
     Keeps, in every row block ``i >= text_blocks_q``, the ``topk`` columns of
-    highest ``mean(q_block_i) . mean(k_block_j)`` (fp64; ties -> lower column),
+    highest ``mean(q_block_i) . mean(k_block_j)`` (fp64; ties -> lower column; NaN
+    ranks above every number, as torch.topk ranks it),
     plus the forced columns ``j < text_blocks_k`` (and ``j == i`` with
     ``force_diag``).  With ``forced_inside_topk`` the forced columns count
     toward ``topk``.  Rows ``i < text_blocks_q`` are dense.

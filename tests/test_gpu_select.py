@@ -110,3 +110,37 @@ def test_integer_inputs_many_ties(cuda_device, S, block, topk, tq, tk, diag, ins
     q = torch.randint(-2, 3, (1, 2, S, d), generator=g).to(torch.bfloat16)
     k = torch.randint(-2, 3, (1, 2, S, d), generator=g).to(torch.bfloat16)
     _check(cuda_device, q, k, block, block, topk, tq=tq, tk=tk, diag=diag, inside=inside)
+
+
+def test_nan_and_inf_blocks_rank_like_torch_topk(cuda_device):
+    """A NaN in a query block makes that row's scores NaN; infinities make
+    +-inf or NaN scores.  NaN ranks above every number (torch.topk's rule,
+    which the reference selects with) and NaNs tie to the lower column, so
+    such rows keep their first k eligible columns.  Masks and CSR must equal
+    the oracle's; scores must agree bit for bit where they are numbers."""
+    g = torch.Generator().manual_seed(12)
+    q = torch.randn(2, 2, 4096, 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(2, 2, 4096, 64, generator=g).to(torch.bfloat16)
+    q[0, 0, 300, 5] = float("nan")
+    q[1, 1, 700, 3] = float("inf")
+    q[0, 1, 1000:1100] = 0
+    k[0, 1, 2000:2200] = 0
+    k[1, 0, 129, 0] = float("-inf")
+    csr = kernels.pool_topk(q.to(cuda_device), k.to(cuda_device), block_m=128, block_n=128, topk=6,
+                            text_blocks_q=1, text_blocks_k=1, return_mask=True, return_scores=True)
+    torch.cuda.synchronize()
+    mask_ref, score_ref = osel.select_blocks(q, k, 128, 128, 6, 1, 1)
+    scores = csr.scores.cpu().numpy()
+    nan = np.isnan(score_ref)
+    assert nan.any() and np.array_equal(np.isnan(scores), nan)
+    assert np.array_equal(scores[~nan].view(np.uint64), score_ref[~nan].view(np.uint64))
+    mask = csr.mask.cpu().numpy().astype(bool)
+    assert np.array_equal(mask, mask_ref), f"{(mask != mask_ref).sum()} mask bits differ"
+    rp_ref, ci_ref = osel.dense_to_csr(mask_ref)
+    rp, ci = csr.row_ptr.cpu().numpy(), csr.col_idx.cpu().numpy()
+    assert np.array_equal(rp, rp_ref)
+    for h in range(rp.shape[0]):
+        assert np.array_equal(ci[rp[h, 0]:rp[h, -1]], ci_ref[rp[h, 0]:rp[h, -1]])
+    # the NaN row (head 0, row block 2): its 6 picks are the lowest columns,
+    # text column 0 among them
+    assert np.array_equal(np.flatnonzero(mask_ref[0, 0, 2]), np.arange(6))
